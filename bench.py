@@ -1,0 +1,453 @@
+"""Benchmark of the 800h hot path on B200: paged GQA decode over the 800h cache at 64 sequences x 32,768 tokens per GPU,
+all 6 attention layers of the LFM3-1.7B shape (4 quantized layers: 127 sub-blocks + a 256-token exact tail; 2 window
+layers: 4 sinks + 256 exact tokens), one decode query per sequence per layer (the metric's
+config).  Sub-blocks and exact pages sit at a seeded random permutation of pool slots.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+A step = the decode of all 6 layers for the rank's 64 sequences (one token per sequence).  `value` = sequences x
+steps x ranks / max-over-ranks device time (tok/s, weak scaling: 64 sequences per GPU).  `e2e` = the same metric
+through the public API with the step's inputs (6 x q, the current token's K / V) copied from pinned host memory, the
+current token written into its exact page, and the 6 outputs read back, all inside the timed region.  `roofline` =
+the quantized-split kernel (the dominant one) timed alone with CUDA events: algorithmic bytes (51,200 per sub-block)
+/ duration against the measured HBM copy bandwidth.  `cpu_baseline` = the CPU oracle (a C port of the reference's
+torch decode, OpenMP over (sequence, kv head)) on 8 of the sequences, all 6 layers, on this host's cores.
+
+--impl reference: the reference's CPU path for this step (the oracle port, all host threads) on a bounded sample of
+the same workload, printed as the reference arm's line; on N > 1 ranks only rank 0 runs it."""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "lfm3-kv800_b200"), ROOT, os.path.join(ROOT, "tests", "golden")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "800h paged-decode tok/s and HBM GB/s (vs 8 TB/s) at 64x32K ctx, 1/2/4/8 B200"
+B_PER_GPU, N_CTX = 64, 32768
+QUANT_LAYERS, WINDOW_LAYERS = 4, 2
+EBS, NSINK, WIN, SUB = 64, 4, 256, 51200
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------- workload (one rank)
+class Layer:
+    """One attention layer's 800h cache for B sequences of n tokens, pages at random pool slots."""
+
+    def __init__(self, kv800, torch, dev, B, n, win, gen, chunk=512):
+        self.win = win
+        self.B, self.n = B, n
+        nq = 0 if win else max(0, n - 128) // 256
+        self.nq = nq
+        lo = nq * 256 if not win else max(0, n - win)
+        self.exact = n - lo
+        npg_row = n // EBS + 1
+        first_pg, last_pg = lo // EBS, (n - 1) // EBS
+        pages_per_seq = last_pg - first_pg + 1
+        npages = B * pages_per_seq
+        perm = torch.randperm(npages + 3, generator=gen)[:npages].view(B, pages_per_seq)
+        self.eoff = torch.zeros(B, npg_row, dtype=torch.int64)
+        self.eoff[:, first_pg:last_pg + 1] = perm * (4 * EBS * 256)
+        self.eoff = self.eoff.to(dev)
+        self.epool = torch.zeros(npages + 3, 4, EBS, 256, dtype=torch.bfloat16, device=dev)
+        # exact tokens [lo, n): written through the library's page scatter
+        seq = torch.arange(B, dtype=torch.int32).repeat_interleave(n - lo).to(dev)
+        pos = torch.arange(lo, n, dtype=torch.int64).repeat(B).to(dev)
+        kk = torch.randn(B * (n - lo), 4, 128, device=dev).to(torch.bfloat16)
+        vv = torch.randn(B * (n - lo), 4, 128, device=dev).to(torch.bfloat16)
+        kv800.write_exact(self.epool, self.eoff, EBS, EBS * 256, 256, 128, kk, vv, seq, pos)
+        if nq:
+            nslot = B * nq + 7
+            slots = torch.randperm(nslot, generator=gen)[:B * nq].view(B, nq)
+            self.boff = (slots * SUB).to(torch.int64).to(dev)
+            self.qpool = torch.empty(nslot, SUB, dtype=torch.uint8, device=dev)
+            flat_slots = slots.reshape(-1).to(dev)
+            for c0 in range(0, B * nq, chunk):
+                c1 = min(c0 + chunk, B * nq)
+                k = torch.randn(c1 - c0, 256, 4, 128, device=dev).to(torch.bfloat16)
+                v = torch.randn(c1 - c0, 256, 4, 128, device=dev).to(torch.bfloat16)
+                self.qpool[flat_slots[c0:c1]] = kv800.quantize_blocks(k, v)
+        else:
+            self.qpool = torch.zeros(1, SUB, dtype=torch.uint8, device=dev)
+            self.boff = torch.zeros(B, 1, dtype=torch.int64, device=dev)
+        if win:
+            self.sk = torch.randn(B, NSINK, 4, 128, device=dev).to(torch.bfloat16)
+            self.sv = torch.randn(B, NSINK, 4, 128, device=dev).to(torch.bfloat16)
+            self.skoff = (torch.arange(B, dtype=torch.int64) * NSINK * 512).to(dev)
+        else:
+            self.sk = self.sv = self.skoff = None
+        self.N = torch.full((B,), n, dtype=torch.int32, device=dev)
+        self.NQ = torch.full((B,), nq, dtype=torch.int32, device=dev)
+        self.P = kv800.Paged(qpool=self.qpool, boff=self.boff, epool=self.epool, eoff=self.eoff, ebs=EBS,
+                             e_hs=EBS * 256, e_ts=256, e_v=128, sk=self.sk, sv=self.sv, skoff=self.skoff,
+                             svoff=self.skoff, N=self.N, NQ=self.NQ, nqmax=nq, win=win)
+
+    def algo_bytes(self):
+        """Cache bytes one decode of this layer must read (the reference's formula, nvidia/check_nvidia.py:563)."""
+        ex = self.exact + (NSINK if self.win else 0)
+        return self.B * (self.nq * 256 * 200 + ex * 2048)
+
+
+def build_workload(kv800, torch, dev, rank, B=B_PER_GPU, n=N_CTX):
+    import inputs as I
+    gen = torch.Generator().manual_seed(1234 + rank)
+    torch.manual_seed(1234 + rank)
+    layers = [Layer(kv800, torch, dev, B, n, 0, gen) for _ in range(QUANT_LAYERS)]
+    layers += [Layer(kv800, torch, dev, B, n, WIN, gen) for _ in range(WINDOW_LAYERS)]
+    cs, sn = I.rope_tables(n + 64)
+    c32 = torch.from_numpy(cs.view(np.int16)).view(torch.bfloat16).to(dev)
+    s32 = torch.from_numpy(sn.view(np.int16)).view(torch.bfloat16).to(dev)
+    qs = [torch.randn(B, 16, 128, device=dev).to(torch.bfloat16) for _ in layers]
+    return layers, qs, c32, s32
+
+
+# ---------------------------------------------------------------- clocks sampled during the timed region
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx, self.proc, self.path = gpu_index, None, None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- CPU oracle on a bounded sample
+def cpu_sample(layers, qs, c32, s32, S, reps=1):
+    """Time the oracle (C port of the reference decode) on sequences [0, S) of every layer; -> (tok/s, sec/step)."""
+    from oracle import oracle as O
+
+    def nb(t):
+        import torch
+        return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+    cs, sn = nb(c32), nb(s32)
+    per_layer = []
+    for L, q in zip(layers, qs):
+        if L.nq:
+            rows = L.boff[:S].cpu().numpy()
+            qpool = L.qpool[(L.boff[:S] // SUB).reshape(-1)].cpu().numpy()
+            boff = (np.arange(S * L.nq, dtype=np.int64) * SUB).reshape(S, L.nq)
+            del rows
+        else:
+            qpool, boff = np.zeros((1, SUB), np.uint8), np.zeros((S, 1), np.int64)
+        P = dict(qpool=qpool, boff=boff, epool=nb(L.epool), eoff=L.eoff[:S].cpu().numpy(), ebs=EBS, e_hs=EBS * 256,
+                 e_ts=256, e_v=128, sk=None if L.sk is None else nb(L.sk), sv=None if L.sv is None else nb(L.sv),
+                 skoff=None if L.skoff is None else L.skoff[:S].cpu().numpy(),
+                 svoff=None if L.skoff is None else L.skoff[:S].cpu().numpy(), N=L.N[:S].cpu().numpy(),
+                 NQ=L.NQ[:S].cpu().numpy(), nqmax=L.nq, win=L.win)
+        per_layer.append((P, nb(q[:S])))
+    best = None
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        for P, q in per_layer:
+            O.decode(P, q, cs, sn)
+        dt = time.perf_counter() - t0
+        best = dt if best is None else min(best, dt)
+    return S / best, best
+
+
+# ---------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="cuda", choices=("cuda", "reference"))
+    ap.add_argument("--cpu-seqs", type=int, default=8, help="sequences of the CPU-baseline sample")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--seqs", type=int, default=B_PER_GPU, help="sequences per GPU (profiling: smaller cases)")
+    ap.add_argument("--ctx", type=int, default=N_CTX, help="context length (profiling: smaller cases)")
+    a = ap.parse_args()
+    a.warmup = max(a.warmup, 3)
+
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    n_gpus = max(world, 1)
+
+    if a.impl == "reference":
+        return reference_arm(a, rank, world, n_gpus)
+
+    from lfm3_kv800 import _lib, kv800
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    layers, qs, c32, s32 = build_workload(kv800, torch, dev, rank, B=a.seqs, n=a.ctx)
+    torch.cuda.synchronize()
+    step_bytes = sum(L.algo_bytes() for L in layers)
+
+    def step():
+        return [kv800.decode(L.P, q, c32, s32) for L, q in zip(layers, qs)]
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        torch.cuda.synchronize()
+        ev0.record()
+        for _ in range(a.steps):
+            step()
+        ev1.record()
+        torch.cuda.synchronize()
+    t = ev0.elapsed_time(ev1) / 1e3
+    if world > 1:
+        tt = torch.tensor([t], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+        dist.barrier()
+    clocks = clk.summary()
+    value = a.seqs * a.steps * n_gpus / t
+    launches_per_step = sum(3 if L.nq else 2 for L in layers)
+
+    # ---- dominant kernel alone: the quantized-split kernel on layer 0, same split as decode()
+    L0 = layers[0]
+    lib = _lib.lib()
+    B = L0.B
+    spb = 0
+    ws_bytes = int(lib.kv800_decode_workspace_size(B, L0.nq, 0, 0))
+    nsl = (ws_bytes - 512) // (B * 16 * 4 * 130)
+    ns = nsl - 4
+    spb = -(-L0.nq // ns)
+    ns = -(-L0.nq // spb)
+    mo = torch.empty(B, ns + 1, 16, device=dev)
+    lo = torch.empty_like(mo)
+    ao = torch.empty(B, ns + 1, 16, 128, device=dev)
+    import ctypes
+    st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    scale = 128 ** -0.5 * kv800.LOG2E
+
+    def qdec():
+        _lib.call("kv800_qdecode", ctypes.c_void_p(qs[0].data_ptr()), ctypes.c_void_p(L0.qpool.data_ptr()),
+                  L0.qpool.numel(), ctypes.c_void_p(L0.boff.data_ptr()), L0.boff.stride(0),
+                  ctypes.c_void_p(L0.NQ.data_ptr()), ctypes.c_void_p(c32.data_ptr()),
+                  ctypes.c_void_p(s32.data_ptr()), c32.shape[0], ctypes.c_void_p(mo.data_ptr()),
+                  ctypes.c_void_p(lo.data_ptr()), ctypes.c_void_p(ao.data_ptr()), B, ns, spb, L0.nq, scale, None, st)
+
+    kreps = 10
+    flushbuf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        qdec()
+    kt = []
+    for _ in range(kreps):
+        flushbuf.fill_(1)                       # evict L2 between timed launches
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        qdec()
+        e1.record()
+        torch.cuda.synchronize()
+        kt.append(e0.elapsed_time(e1) / 1e3)
+    kdur = statistics.median(kt)
+    kbytes = B * L0.nq * SUB
+    hbm, peak_kind = peaks()
+    roofline = {"bound": "hbm", "achieved": round(kbytes / kdur / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(kbytes / kdur / 1e9 / hbm, 4), "traffic": None, "peak_source": peak_kind,
+                "kernel": "qdecode_simt", "bytes_per_launch": kbytes, "launch_us": round(kdur * 1e6, 1)}
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not a.no_e2e:
+        nl = len(layers)
+        hq = [q.cpu().pin_memory() for q in qs]
+        hk = torch.randn(nl, B, 4, 128).to(torch.bfloat16).pin_memory()
+        hv = torch.randn(nl, B, 4, 128).to(torch.bfloat16).pin_memory()
+        hout = [torch.empty(B, 16, 128, dtype=torch.bfloat16).pin_memory() for _ in layers]
+        seqs = torch.arange(B, dtype=torch.int32, device=dev)
+        posv = torch.full((B,), a.ctx - 1, dtype=torch.int64, device=dev)
+
+        def e2e_step():
+            for i, L in enumerate(layers):
+                q = hq[i].to(dev, non_blocking=True)
+                k = hk[i].to(dev, non_blocking=True)
+                v = hv[i].to(dev, non_blocking=True)
+                kv800.write_exact(L.epool, L.eoff, EBS, EBS * 256, 256, 128, k, v, seqs, posv)
+                o = kv800.decode(L.P, q, c32, s32)
+                hout[i].copy_(o, non_blocking=True)
+            return hout
+
+        for _ in range(a.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        te = e0.elapsed_time(e1) / 1e3
+        if world > 1:
+            tt = torch.tensor([te], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            te = float(tt.item())
+        h2d = sum(x.numel() * x.element_size() for x in hq) + hk.numel() * 2 + hv.numel() * 2
+        d2h = sum(x.numel() * x.element_size() for x in hout)
+        e2e = {"value": round(a.seqs * a.steps * n_gpus / te, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": round(te / a.steps * 1e3, 4)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu:
+        S = a.cpu_seqs
+        tps, sec = cpu_sample(layers, qs, c32, s32, S)
+        cpu = {"value": round(tps, 2), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{S} of the 64 sequences x 32,768 tokens, all 6 layers, oracle/kv800_oracle.c "
+                         f"(OpenMP over sequence x kv head), one pass of {sec:.2f} s"}
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": n_gpus, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": round(t / a.steps * 1e3, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "u8+bf16 (fp32 math)", "data": "synthetic",
+                "config": {"workload": "config 3: 64 seq x 32768 ctx per GPU, 4 quantized (127 sub-blocks + 256 "
+                                       "exact) + 2 window (4 sinks + 256) layers, 16q/4kv/128, shuffled pages",
+                           "seqs_per_gpu": a.seqs, "ctx": a.ctx, "layers": QUANT_LAYERS + WINDOW_LAYERS,
+                           "parallelism": f"dp{n_gpus} (sequence sharding, no collective)",
+                           "l2": "inputs larger than L2 (1.87 GB per step); kernel timing flushes L2 per launch"},
+                "hbm_gbs_step": round(step_bytes * a.steps / t / 1e9, 1),
+                "hbm_frac_step": round(step_bytes * a.steps / t / 1e9 / peaks()[0], 4),
+                "bytes_per_step_per_gpu": step_bytes, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": launches_per_step * a.steps, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+
+
+def reference_arm(a, rank, world, n_gpus):
+    """The reference's CPU path for this step (the oracle port of torch_decode, all host threads) on a bounded sample:
+    S sequences of the 64 x 32K, 6-layer workload per step, K steps after W warm-ups."""
+    if rank != 0:
+        return
+    import torch
+    from oracle import oracle as O
+    O.lib()
+    S = 4
+    # the workload built on the CPU side with the oracle's own quantizer (no GPU used by this arm)
+    rs = np.random.RandomState(99)
+    import inputs as I
+    cs, sn = I.rope_tables(N_CTX + 64)
+    per_layer = []
+    for li in range(QUANT_LAYERS + WINDOW_LAYERS):
+        win = 0 if li < QUANT_LAYERS else WIN
+        nq = 0 if win else (N_CTX - 128) // 256
+        lo = nq * 256 if not win else N_CTX - win
+        npg = N_CTX // EBS + 1
+        first = lo // EBS
+        pps = (N_CTX - 1) // EBS - first + 1
+        epool = np.zeros((S * pps, 4, EBS, 256), np.uint16)
+        eoff = np.zeros((S, npg), np.int64)
+        eoff[:, first:first + pps] = (rs.permutation(S * pps).reshape(S, pps) * 4 * EBS * 256)
+        epool[...] = I.f32_to_bf16(rs.standard_normal(epool.shape).astype(np.float32))
+        if nq:
+            M = S * nq
+            qpool = np.zeros((M, SUB), np.uint8)
+            for c0 in range(0, M, 64):
+                c1 = min(M, c0 + 64)
+                k = I.f32_to_bf16(rs.standard_normal((c1 - c0, 256, 4, 128)).astype(np.float32))
+                v = I.f32_to_bf16(rs.standard_normal((c1 - c0, 256, 4, 128)).astype(np.float32))
+                qpool[c0:c1] = O.quantize_blocks(k, v)
+            boff = (rs.permutation(M).reshape(S, nq) * SUB).astype(np.int64)
+        else:
+            qpool, boff = np.zeros((1, SUB), np.uint8), np.zeros((S, 1), np.int64)
+        sk = I.f32_to_bf16(rs.standard_normal((S, NSINK, 4, 128)).astype(np.float32)) if win else None
+        P = dict(qpool=qpool, boff=boff, epool=epool, eoff=eoff, ebs=EBS, e_hs=EBS * 256, e_ts=256, e_v=128, sk=sk,
+                 sv=sk, skoff=np.arange(S, dtype=np.int64) * NSINK * 512, svoff=np.arange(S, dtype=np.int64) * NSINK * 512,
+                 N=np.full(S, N_CTX, np.int32), NQ=np.full(S, nq, np.int32), nqmax=nq, win=win)
+        q = I.f32_to_bf16(rs.standard_normal((S, 16, 128)).astype(np.float32))
+        per_layer.append((P, q))
+
+    def step():
+        for P, q in per_layer:
+            O.decode(P, q, cs, sn)
+
+    for _ in range(min(a.warmup, 1)):
+        step()
+    steps = max(1, min(a.steps, 3))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = (time.perf_counter() - t0) / steps
+    v = S / dt
+    cores = os.cpu_count()
+    line = {"metric": METRIC, "value": round(v, 2), "unit": "tok/s", "n_gpus": n_gpus, "steps": steps,
+            "warmup": min(a.warmup, 1), "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8+bf16 (fp32 math)", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "config 3: 64 seq x 32768 ctx per GPU, 4 quantized (127 sub-blocks + 256 exact) + "
+                                   "2 window (4 sinks + 256) layers, 16q/4kv/128, shuffled pages",
+                       "seqs_per_gpu": B_PER_GPU, "ctx": N_CTX, "layers": QUANT_LAYERS + WINDOW_LAYERS,
+                       "parallelism": "host cores (reference CPU path)"},
+            "cpu_baseline": {"value": round(v, 2), "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": f"{S} sequences x 32,768 tokens x 6 layers per step (of the 64 per GPU), "
+                                       f"oracle/kv800_oracle.c decode with OpenMP over sequence x kv head"},
+            "e2e": {"value": round(v, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,142 @@
+/*
+ * kv800_b200.h -- C ABI of the B200 (sm_100a) implementation of lfm3_kv800's 800h hot path:
+ *   the 800h quantizer / flush (256-token sub-blocks of 51,200 bytes: 2-bit pre-RoPE K per channel, 1-bit
+ *   Hadamard-rotated V per token, fp8 e4m3 lo / scale) and paged GQA decode attention over those sub-blocks plus the
+ *   exact bf16 tail (16 query heads, 4 KV heads, head_dim 128).
+ *
+ * Conventions (the reference's, lfm3_kv800/kv800.py:1-16):
+ *   - every buffer is caller-owned device memory; the library allocates nothing (scratch is passed in);
+ *   - pool offsets are int64 and relative to the pool pointer passed in: BOFF in BYTES from `qpool`, EOFF / SKOFF /
+ *     SVOFF in bf16 ELEMENTS from `epool` / `sk` / `sv`;
+ *   - exact page layout: K of (head h, slot t) at eoff + h*e_hs + t*e_ts, V at + e_v (elements);
+ *   - bf16 tensors are passed as uint16_t bit patterns, fp8 bytes as uint8_t;
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream); every call only enqueues work on it;
+ *   - return value: KV800_OK or an error code; kv800_last_error() gives a message for the calling host thread.
+ * Device-side checks: each kernel compares every page / sub-block offset it reads against the pool extent passed in
+ * (bytes / elements) and skips an out-of-range one instead of reading it; the first such event is recorded in the
+ * status word of the workspace (decode) or reported through kv800_check_status (see below).
+ */
+#ifndef KV800_B200_H
+#define KV800_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KV800_API __attribute__((visibility("default")))
+#else
+#define KV800_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KV800_OK 0
+#define KV800_ERR_ARG 1      /* a null pointer, a negative size, a shape outside the supported set */
+#define KV800_ERR_RANGE 2    /* a size above a stated maximum */
+#define KV800_ERR_CUDA 3     /* a CUDA runtime error (launch, configuration) */
+#define KV800_ERR_DEVICE 4   /* a device-side check fired: an offset outside its pool (see kv800_check_status) */
+
+/* ABI revision of this header (bumped on any signature change). */
+KV800_API int kv800_abi_version(void);
+
+/* Message for the last error returned on the calling host thread ("" if none). */
+KV800_API const char* kv800_last_error(void);
+
+/* Layout constants (kv800.py:32-34): BLK 256, SUB 51200, LAG 128, NSINK 4, WIN 256. */
+KV800_API int kv800_constants(int64_t* blk, int64_t* sub, int64_t* lag, int64_t* nsink, int64_t* win);
+
+/*
+ * kv800_quantize_blocks -- replaces kv800.quantize_blocks(k, v, H) (lfm3_kv800/kv800.py:56-76).
+ * k, v: (M, 256, 4, 128) bf16, contiguous (pre-RoPE K, unrotated V); out: (M, 51200) u8.  Bit-exact with the
+ * reference: K lo / hi over 256 tokens per (head, channel), fp8 lo and (hi - lo) / 3 scale, RNE codes; V rotated by
+ * the normalized 128-point Hadamard as a sequential fp32 FMA chain, lo / hi per (token, 2-head group), 1-bit codes.
+ */
+KV800_API int kv800_quantize_blocks(const uint16_t* k, const uint16_t* v, int64_t M, uint8_t* out, void* stream);
+
+/*
+ * kv800_dequantize_blocks -- replaces kv800.dequantize_blocks(sb, H) (lfm3_kv800/kv800.py:79-92).
+ * sb: (M, 51200) u8, contiguous; k_out: (M, 256, 4, 128) bf16 = bf16(codes * ksc + klo) (pre-RoPE);
+ * v_out: (M, 256, 4, 128) f32 = (bits * vsc + vlo) @ H (unrotated V), the same FMA chain as the quantizer.
+ */
+KV800_API int kv800_dequantize_blocks(const uint8_t* sb, int64_t M, uint16_t* k_out, float* v_out, void* stream);
+
+/*
+ * kv800_flush -- replaces the flush of PagedStore.append (kv800.py:433-440) and of the vLLM backend
+ * (vllm_attn.py:298-317): for m < M, gather the 256 exact tokens of sub-block blk[m] of sequence seq[m] (positions
+ * [256 blk, 256 blk + 256)) from the exact pages, quantize them as kv800_quantize_blocks does, and write the 51,200
+ * bytes at qpool + boff[seq * boff_stride + blk].  seq / blk are device int32 arrays of length M; nseq is the
+ * number of rows of the eoff / boff tables (0 <= seq < nseq, 0 <= blk < boff_stride are checked on the device).
+ * epool_elems / qpool_bytes: pool extents used by the device-side range checks.  status: optional device int
+ * (NULL = none) set to nonzero when a range check fires.
+ */
+KV800_API int kv800_flush(const uint16_t* epool, int64_t epool_elems, const int64_t* eoff, int64_t eoff_stride, int64_t ebs,
+                int64_t e_hs, int64_t e_ts, int64_t e_v, uint8_t* qpool, int64_t qpool_bytes, const int64_t* boff,
+                int64_t boff_stride, const int32_t* seq, const int32_t* blk, int64_t M, int64_t nseq, int* status,
+                void* stream);
+
+/*
+ * kv800_write_exact -- replaces the exact-page scatter of PagedStore.append (kv800.py:423-428) and of the vLLM
+ * backend (vllm_attn.py:261-269): token i (i < T) of k / v ((T, 4, 128) bf16, contiguous) goes to sequence seq[i],
+ * position pos[i]: K at epool + eoff[seq * eoff_stride + pos / ebs] + h*e_hs + (pos % ebs)*e_ts, V at + e_v.
+ * seq (int32) and pos (int64) are device arrays of length T.
+ */
+KV800_API int kv800_write_exact(uint16_t* epool, int64_t epool_elems, const int64_t* eoff, int64_t eoff_stride, int64_t ebs,
+                      int64_t e_hs, int64_t e_ts, int64_t e_v, const uint16_t* k, const uint16_t* v,
+                      const int32_t* seq, const int64_t* pos, int64_t T, int64_t nseq, int* status, void* stream);
+
+/*
+ * Paged decode.  The record below carries the reference's Paged slots (kv800.py:239-248); pointers are device
+ * pointers.  sk / sv / skoff / svoff may be NULL (no sinks).  win = 0: quantized layer, sub-blocks j < min(NQ[b],
+ * nqmax) plus exact positions [256 NQ[b], N[b]); win > 0: window layer, exact positions [max(256 NQ[b], N[b] - win),
+ * N[b]) plus the sinks (positions < min(nsink, lo, N[b])) when sk is set.
+ */
+typedef struct kv800_paged {
+    const uint8_t* qpool; int64_t qpool_bytes;
+    const int64_t* boff; int64_t boff_stride;
+    const uint16_t* epool; int64_t epool_elems;
+    const int64_t* eoff; int64_t eoff_stride;
+    int64_t ebs, e_hs, e_ts, e_v;
+    const uint16_t* sk; const uint16_t* sv; int64_t sk_elems, sv_elems;
+    const int64_t* skoff; const int64_t* svoff;
+    const int32_t* N; const int32_t* NQ;
+    int64_t nqmax;          /* host bound >= max(NQ) (the reference's host int) */
+    int64_t win;            /* 0 or the window (256) */
+    int64_t nsink;          /* sinks read when win > 0 and sk != NULL (the reference's NSINK = 4) */
+} kv800_paged;
+
+/*
+ * kv800_decode -- replaces kv800.decode(P, q, cos_t, sin_t, H, spb, target) (kv800.py:330-383) with one CUDA
+ * backend.  q: (B, 16, 128) bf16 post-RoPE; cos_t / sin_t: (npos, 32) bf16 tables of the 32 rotating frequency pairs
+ * (dims d and d + 64 share frequency d, d < 32); out: (B, 16, 128) bf16.  spb: sub-blocks per split (<= 0: chosen by
+ * the library).  workspace: device scratch of kv800_decode_workspace_size(...) bytes, 256-byte aligned; its first
+ * int is the device status word (0 = clean; set when a range check fires).
+ */
+KV800_API int64_t kv800_decode_workspace_size(int64_t B, int64_t nqmax, int64_t win, int64_t spb);
+KV800_API int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t, const uint16_t* sin_t,
+                 int64_t npos, int64_t B, int64_t spb, uint16_t* out, void* workspace, int64_t workspace_bytes,
+                 void* stream);
+
+/*
+ * The reference's three native decode ops (kv800::qdecode / xdecode / combine, csrc/kv800_sycl.sycl:554-561) with
+ * the same argument meaning and partial layout: MO / LO (B, ns + 1, 16) f32, AO (B, ns + 1, 16, 128) f32; slots
+ * [0, ns) are the quantized splits (V accumulated in the Hadamard domain), slot ns the sinks + exact tokens.
+ * scale = 128^-0.5 * log2(e).  combine writes (B, 16, 128) bf16 into out.
+ */
+KV800_API int kv800_qdecode(const uint16_t* q, const uint8_t* qpool, int64_t qpool_bytes, const int64_t* boff,
+                  int64_t boff_stride, const int32_t* NQ, const uint16_t* cos_t, const uint16_t* sin_t, int64_t npos,
+                  float* mo, float* lo, float* ao, int64_t B, int64_t ns, int64_t spb, int64_t nqmax, float scale,
+                  int* status, void* stream);
+KV800_API int kv800_xdecode(const uint16_t* q, const kv800_paged* P, const uint16_t* cos_t, const uint16_t* sin_t,
+                  int64_t npos, float* mo, float* lo, float* ao, int64_t B, int64_t ns, float scale, int* status,
+                  void* stream);
+KV800_API int kv800_combine(const float* mo, const float* lo, const float* ao, int64_t B, int64_t ns, uint16_t* out,
+                  void* stream);
+
+/* Copy the device status word at `status` to *host_value (synchronizes the stream). */
+KV800_API int kv800_check_status(const int* status, int* host_value, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KV800_B200_H */

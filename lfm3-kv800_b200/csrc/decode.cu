@@ -1,0 +1,598 @@
+// 800h paged GQA decode on sm_100a -- SIMT kernels: split partials over quantized sub-blocks (qdecode), over sinks +
+// exact bf16 tokens (xdecode), and the log-sum-exp merge with the in-register Hadamard (combine).
+//
+// Semantics follow the reference's torch decode (lfm3_kv800/torch_decode.py:16-80), including its two bf16 roundings
+// of every key: the dequantized pre-RoPE key is rounded to bf16 (kv800.py:86) and the rotated key is rounded to bf16
+// again (torch_decode.py:24).  Both are reproduced exactly: c * sc + lo is exact in fp32 for fp8 sc / lo and c <= 3,
+// so one FMA gives the reference's fp32 value; k0 * cs and k2 * sn are exact in fp32 (bf16 x bf16), so
+// fma(k0, cs, -(k2 * sn)) is the reference's fl(fl(k0 cs) - fl(k2 sn)).  Partials use the reference's split layout
+// (kv800.py:362-383): per (row b, slot) m (log2 domain), l and acc (16 x 128, fp32); quantized slots keep V in the
+// Hadamard domain and combine() rotates their weighted sum once (kv800.py:231-236).
+#include "kv800_common.cuh"
+
+namespace kv800 {
+
+constexpr float NEG_BIG = -1e30f;   // the reference's initial running max (kv800.py:127)
+
+struct QArgs {
+    const uint16_t* q;
+    const uint8_t* qpool;
+    int64_t qpool_bytes;
+    const int64_t* boff;
+    int64_t boff_stride;
+    const int32_t* NQ;
+    int64_t nqmax;
+    const uint16_t* cos_t;
+    const uint16_t* sin_t;
+    int64_t npos;
+    float* mo;
+    float* lo;
+    float* ao;
+    int nslots;   // slots per row in mo / lo / ao
+    int spb;      // sub-blocks per split
+    float scale;  // 128^-0.5 * log2(e)
+    int* status;
+};
+
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+    return x;
+}
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+}
+
+// 1 + c / 4 as fp32 for a 2-bit code c (mantissa bits 21-22): k = fma(x, 4 sc, lo - 4 sc) is c * sc + lo exactly.
+__device__ __forceinline__ float code_x(uint32_t byte, int plane) {
+    return __uint_as_float(0x3f800000u | (((byte >> (2 * plane)) & 3u) << 21));
+}
+
+// Rotated bf16 key pair of the reference: kr0 = bf16(k0 cs - k2 sn), kr2 = bf16(k2 cs + k0 sn).
+__device__ __forceinline__ void rope_pair(float k0, float k2, float cs, float sn, float& r0, float& r2) {
+    r0 = bfround(fmaf(k0, cs, -(k2 * sn)));
+    r2 = bfround(fmaf(k2, cs, k0 * sn));
+}
+
+// grid (B, ns), block 128: warp h = kv head h, lane = token of a 32-token tile (QK) / dims lane + 32 k (PV).
+__global__ void __launch_bounds__(128) qdecode_simt(QArgs a) {
+    const int b = blockIdx.x, s = blockIdx.y, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ float4 qs[HEADS][32][4];        // [h][j][r] = q[r][j + 32 p] for p = x, y, z, w
+    __shared__ float kA[HEADS][DIM], kB[HEADS][DIM];
+    __shared__ float4 pvs[HEADS][32];          // p * vs of token tt for the 4 rows
+    __shared__ uint4 vbs[HEADS][32];           // 16 bytes of V bits of token tt
+    for (int i = lane; i < 4 * 32; i += 32) {
+        const int r = i >> 5, j = i & 31;
+        const uint16_t* qr = a.q + ((int64_t)b * QROWS + h * 4 + r) * DIM;
+        qs[h][j][r] = make_float4(bf2f(qr[j]), bf2f(qr[j + 32]), bf2f(qr[j + 64]), bf2f(qr[j + 96]));
+    }
+    float m[4], l_lane[4], lv_lane[4], acc[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        m[r] = NEG_BIG;
+        l_lane[r] = lv_lane[r] = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; k++) acc[r][k] = 0.f;
+    }
+    int64_t nq = a.NQ[b];
+    if (nq > a.nqmax) nq = a.nqmax;
+    const int64_t j0 = (int64_t)s * a.spb;
+    const int64_t j1 = min(j0 + a.spb, nq);
+    __syncwarp();
+    for (int64_t jb = j0; jb < j1; jb++) {
+        if (jb >= a.boff_stride) {
+            if (lane == 0) flag(a.status, ST_TABLE);
+            break;
+        }
+        const int64_t off = a.boff[(int64_t)b * a.boff_stride + jb];
+        const uint8_t* sb = a.qpool + off;
+        if (off < 0 || off + SUB > a.qpool_bytes || (reinterpret_cast<uintptr_t>(sb) & 15u)) {
+            if (lane == 0) flag(a.status, ST_QPOOL);
+            continue;
+        }
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            const int c = lane + 32 * p;
+            const float sc = f8dec(sb[KSC_O + h * DIM + c]), l8 = f8dec(sb[KLO_O + h * DIM + c]);
+            kA[h][c] = 4.0f * sc;
+            kB[h][c] = l8 - 4.0f * sc;
+        }
+        __syncwarp();
+        for (int t0 = 0; t0 < BLK; t0 += 32) {
+            const int t = t0 + lane;
+            const int64_t pos = jb * BLK + t;
+            const uint4* kp = reinterpret_cast<const uint4*>(sb + KC_O + (t * HEADS + h) * 32);
+            uint4 kw0 = kp[0], kw1 = kp[1];
+            uint32_t kw[8] = {kw0.x, kw0.y, kw0.z, kw0.w, kw1.x, kw1.y, kw1.z, kw1.w};
+            uint32_t cw[16], sw[16];
+            if (pos < a.npos) {
+                const uint4* cp = reinterpret_cast<const uint4*>(a.cos_t + pos * 32);
+                const uint4* sp = reinterpret_cast<const uint4*>(a.sin_t + pos * 32);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    uint4 c4 = cp[i], s4 = sp[i];
+                    cw[4 * i] = c4.x; cw[4 * i + 1] = c4.y; cw[4 * i + 2] = c4.z; cw[4 * i + 3] = c4.w;
+                    sw[4 * i] = s4.x; sw[4 * i + 1] = s4.y; sw[4 * i + 2] = s4.z; sw[4 * i + 3] = s4.w;
+                }
+            } else {
+                flag(a.status, ST_TABLE);
+#pragma unroll
+                for (int i = 0; i < 16; i++) cw[i] = sw[i] = 0u;
+            }
+            float sc4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                const uint32_t byte = (kw[j >> 2] >> (8 * (j & 3))) & 0xffu;
+                const float k0 = bfround(fmaf(code_x(byte, 0), kA[h][j], kB[h][j]));
+                const float k1 = bfround(fmaf(code_x(byte, 1), kA[h][j + 32], kB[h][j + 32]));
+                const float k2 = bfround(fmaf(code_x(byte, 2), kA[h][j + 64], kB[h][j + 64]));
+                const float k3 = bfround(fmaf(code_x(byte, 3), kA[h][j + 96], kB[h][j + 96]));
+                const uint32_t cword = cw[j >> 1], sword = sw[j >> 1];
+                const float cs = __uint_as_float((j & 1) ? (cword & 0xffff0000u) : (cword << 16));
+                const float sn = __uint_as_float((j & 1) ? (sword & 0xffff0000u) : (sword << 16));
+                float r0, r2;
+                rope_pair(k0, k2, cs, sn, r0, r2);
+#pragma unroll
+                for (int r = 0; r < 4; r++) {
+                    const float4 qv = qs[h][j][r];
+                    sc4[r] = fmaf(qv.x, r0, sc4[r]);
+                    sc4[r] = fmaf(qv.y, k1, sc4[r]);
+                    sc4[r] = fmaf(qv.z, r2, sc4[r]);
+                    sc4[r] = fmaf(qv.w, k3, sc4[r]);
+                }
+            }
+            const float vl = f8dec(sb[VLO_O + t * 2 + (h >> 1)]), vs = f8dec(sb[VSC_O + t * 2 + (h >> 1)]);
+            float alpha[4], p[4];
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                const float s2 = sc4[r] * a.scale;
+                const float mn = fmaxf(m[r], warp_max(s2));
+                alpha[r] = exp2f(m[r] - mn);
+                p[r] = exp2f(s2 - mn);
+                m[r] = mn;
+                l_lane[r] = fmaf(l_lane[r], alpha[r], p[r]);
+                lv_lane[r] = fmaf(lv_lane[r], alpha[r], p[r] * vl);
+            }
+            pvs[h][lane] = make_float4(p[0] * vs, p[1] * vs, p[2] * vs, p[3] * vs);
+            vbs[h][lane] = *reinterpret_cast<const uint4*>(sb + VB_O + (t * HEADS + h) * 16);
+            __syncwarp();
+#pragma unroll
+            for (int r = 0; r < 4; r++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) acc[r][k] *= alpha[r];
+            const int jb8 = lane & 15, sh = lane >> 4;
+            for (int tt = 0; tt < 32; tt++) {
+                const float4 pv = pvs[h][tt];
+                const uint32_t byte = reinterpret_cast<const uint8_t*>(&vbs[h][tt])[jb8];
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const float bit = (float)((byte >> (sh + 2 * k)) & 1u);
+                    acc[0][k] = fmaf(bit, pv.x, acc[0][k]);
+                    acc[1][k] = fmaf(bit, pv.y, acc[1][k]);
+                    acc[2][k] = fmaf(bit, pv.z, acc[2][k]);
+                    acc[3][k] = fmaf(bit, pv.w, acc[3][k]);
+                }
+            }
+            __syncwarp();
+        }
+    }
+    const int64_t slot = (int64_t)b * a.nslots + s;
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        const float l = warp_sum(l_lane[r]), lv = warp_sum(lv_lane[r]);
+        const int64_t row = slot * QROWS + h * 4 + r;
+        if (lane == 0) {
+            a.mo[row] = m[r];
+            a.lo[row] = l;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++) a.ao[row * DIM + lane + 32 * k] = acc[r][k] + lv;
+    }
+}
+
+struct XArgs {
+    const uint16_t* q;
+    kv800_paged P;
+    const uint16_t* cos_t;
+    const uint16_t* sin_t;
+    int64_t npos;
+    float* mo;
+    float* lo;
+    float* ao;
+    int nslots;   // slots per row
+    int slot0;    // first exact slot (= ns)
+    int nx;       // exact splits per row
+    float scale;
+    int* status;
+};
+
+// grid (B, nx), block 128: warp = kv head; split e of row b covers exact tokens [e ch, (e + 1) ch) of the row's
+// sinks + exact positions (sinks first, split 0 only).
+__global__ void __launch_bounds__(128) xdecode_simt(XArgs a) {
+    const int b = blockIdx.x, e = blockIdx.y, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const kv800_paged& P = a.P;
+    __shared__ float4 qx[HEADS][DIM];           // [h][d] = q rows 0..3 at dim d
+    __shared__ float4 ps[HEADS][32];            // p of token tt for the 4 rows
+    __shared__ const uint16_t* vrow[HEADS][32]; // V row of token tt (nullptr = invalid)
+    for (int d = lane; d < DIM; d += 32) {
+        const uint16_t* qr = a.q + ((int64_t)b * QROWS + h * 4) * DIM + d;
+        qx[h][d] = make_float4(bf2f(qr[0]), bf2f(qr[DIM]), bf2f(qr[2 * DIM]), bf2f(qr[3 * DIM]));
+    }
+    const int64_t n = P.N[b], nqb = P.NQ[b];
+    int64_t lo_e = nqb * BLK;
+    if (P.win && n - P.win > lo_e) lo_e = n - P.win;
+    int64_t cnt = 0;
+    if (P.win && P.sk) {
+        cnt = P.nsink;
+        if (lo_e < cnt) cnt = lo_e;
+        if (n < cnt) cnt = n;
+        if (cnt < 0) cnt = 0;
+    }
+    const int64_t E = n > lo_e ? n - lo_e : 0;            // exact positions [lo_e, n)
+    const int64_t ch = (E + a.nx - 1) / a.nx;
+    const int64_t x0 = min((int64_t)e * ch, E), x1 = min(x0 + ch, E);
+    const int64_t s0 = (e == 0) ? 0 : cnt;                 // token list of this split: [s0, cnt) sinks + exact
+    const int64_t total = (cnt - s0) + (x1 - x0);
+    float m[4], l_lane[4], acc[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        m[r] = NEG_BIG;
+        l_lane[r] = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; k++) acc[r][k] = 0.f;
+    }
+    __syncwarp();
+    for (int64_t t0 = 0; t0 < total; t0 += 32) {
+        const int64_t ti = t0 + lane;
+        const uint16_t* kr = nullptr;
+        const uint16_t* vr = nullptr;
+        int64_t pos = 0;
+        if (ti < total) {
+            if (ti < cnt - s0) {
+                const int64_t t = s0 + ti;
+                pos = t;
+                const int64_t ko = P.skoff[b] + (t * HEADS + h) * DIM, vo = P.svoff[b] + (t * HEADS + h) * DIM;
+                if (ko >= 0 && ko + DIM <= P.sk_elems && vo >= 0 && vo + DIM <= P.sv_elems) {
+                    kr = P.sk + ko;
+                    vr = P.sv + vo;
+                } else {
+                    flag(a.status, ST_SINK);
+                }
+            } else {
+                pos = lo_e + x0 + (ti - (cnt - s0));
+                if (pos / P.ebs < P.eoff_stride) {
+                    const int64_t ko = P.eoff[(int64_t)b * P.eoff_stride + pos / P.ebs] + h * P.e_hs + (pos % P.ebs) * P.e_ts;
+                    if (ko >= 0 && ko + DIM <= P.epool_elems && ko + P.e_v >= 0 && ko + P.e_v + DIM <= P.epool_elems) {
+                        kr = P.epool + ko;
+                        vr = P.epool + ko + P.e_v;
+                    } else {
+                        flag(a.status, ST_EPOOL);
+                    }
+                } else {
+                    flag(a.status, ST_TABLE);
+                }
+            }
+            if (kr && pos >= a.npos) {
+                flag(a.status, ST_TABLE);
+                kr = vr = nullptr;
+            }
+        }
+        float s2[4];
+        if (kr) {
+            float kv[DIM];
+#pragma unroll
+            for (int d = 0; d < DIM; d++) kv[d] = bf2f(kr[d]);
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                const float cs = bf2f(a.cos_t[pos * 32 + j]), sn = bf2f(a.sin_t[pos * 32 + j]);
+                float r0, r2;
+                rope_pair(kv[j], kv[j + 64], cs, sn, r0, r2);
+                kv[j] = r0;
+                kv[j + 64] = r2;
+            }
+            float sc4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int d = 0; d < DIM; d++) {
+                const float4 qv = qx[h][d];
+                sc4[0] = fmaf(qv.x, kv[d], sc4[0]);
+                sc4[1] = fmaf(qv.y, kv[d], sc4[1]);
+                sc4[2] = fmaf(qv.z, kv[d], sc4[2]);
+                sc4[3] = fmaf(qv.w, kv[d], sc4[3]);
+            }
+#pragma unroll
+            for (int r = 0; r < 4; r++) s2[r] = sc4[r] * a.scale;
+        } else {
+#pragma unroll
+            for (int r = 0; r < 4; r++) s2[r] = -__int_as_float(0x7f800000);
+        }
+        float alpha[4], p[4];
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const float mn = fmaxf(m[r], warp_max(s2[r]));
+            alpha[r] = exp2f(m[r] - mn);
+            p[r] = exp2f(s2[r] - mn);
+            m[r] = mn;
+            l_lane[r] = fmaf(l_lane[r], alpha[r], p[r]);
+        }
+        ps[h][lane] = make_float4(p[0], p[1], p[2], p[3]);
+        vrow[h][lane] = vr;
+        __syncwarp();
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) acc[r][k] *= alpha[r];
+        const int nt = (int)min((int64_t)32, total - t0);
+        for (int tt = 0; tt < nt; tt++) {
+            const uint16_t* v = vrow[h][tt];
+            if (!v) continue;
+            const float4 pv = ps[h][tt];
+            float x[4];
+            if ((reinterpret_cast<uintptr_t>(v) & 7u) == 0) {
+                const uint2 w = *reinterpret_cast<const uint2*>(v + 4 * lane);
+                x[0] = __uint_as_float(w.x << 16);
+                x[1] = __uint_as_float(w.x & 0xffff0000u);
+                x[2] = __uint_as_float(w.y << 16);
+                x[3] = __uint_as_float(w.y & 0xffff0000u);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; k++) x[k] = bf2f(v[4 * lane + k]);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                acc[0][k] = fmaf(pv.x, x[k], acc[0][k]);
+                acc[1][k] = fmaf(pv.y, x[k], acc[1][k]);
+                acc[2][k] = fmaf(pv.z, x[k], acc[2][k]);
+                acc[3][k] = fmaf(pv.w, x[k], acc[3][k]);
+            }
+        }
+        __syncwarp();
+    }
+    const int64_t slot = (int64_t)b * a.nslots + a.slot0 + e;
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        const float l = warp_sum(l_lane[r]);
+        const int64_t row = slot * QROWS + h * 4 + r;
+        if (lane == 0) {
+            a.mo[row] = m[r];
+            a.lo[row] = l;
+        }
+        *reinterpret_cast<float4*>(a.ao + row * DIM + 4 * lane) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    }
+}
+
+// grid (B), block 512: warp = query row r; lane = dims 4 lane .. 4 lane + 3.  Slots [0, ns) are quantized (Hadamard
+// domain), [ns, nslots) exact.  o = (sum_{s<ns} w_s acc_s) H + sum_{s>=ns} w_s acc_s, w_s = exp2(m_s - max m),
+// out = bf16(o / sum_s w_s l_s) (kv800.py:231-236); a row with no keys at all gives zeros (torch_decode.py:71-72).
+__global__ void __launch_bounds__(512) combine_kernel(const float* mo, const float* lo, const float* ao, int ns,
+                                                      int nslots, uint16_t* out) {
+    const int b = blockIdx.x, r = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float M = NEG_BIG;
+    for (int s = 0; s < nslots; s++) M = fmaxf(M, mo[((int64_t)b * nslots + s) * QROWS + r]);
+    float L = 0.f, oq[4] = {0.f, 0.f, 0.f, 0.f}, oe[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < nslots; s++) {
+        const int64_t row = ((int64_t)b * nslots + s) * QROWS + r;
+        const float w = exp2f(mo[row] - M);
+        L = fmaf(w, lo[row], L);
+        const float4 x = *reinterpret_cast<const float4*>(ao + row * DIM + 4 * lane);
+        float* o = s < ns ? oq : oe;
+        o[0] = fmaf(w, x.x, o[0]);
+        o[1] = fmaf(w, x.y, o[1]);
+        o[2] = fmaf(w, x.z, o[2]);
+        o[3] = fmaf(w, x.w, o[3]);
+    }
+    if (ns > 0) {
+        // 128-point Sylvester Hadamard: dims d = 4 lane + e; stages 1, 2 in-lane, 4 .. 64 across lanes 1 .. 16
+        float a0 = oq[0] + oq[1], a1 = oq[0] - oq[1], a2 = oq[2] + oq[3], a3 = oq[2] - oq[3];
+        oq[0] = a0 + a2; oq[2] = a0 - a2; oq[1] = a1 + a3; oq[3] = a1 - a3;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const bool upper = (lane & o) != 0;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float other = __shfl_xor_sync(0xffffffffu, oq[e], o);
+                oq[e] = upper ? other - oq[e] : oq[e] + other;
+            }
+        }
+        const float c = 0.0883883461356163f;
+#pragma unroll
+        for (int e = 0; e < 4; e++) oe[e] = fmaf(oq[e], c, oe[e]);
+    }
+    uint16_t res[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) res[e] = (L > 0.f) ? f2bf(oe[e] / L) : (uint16_t)0;
+    uint2 pk;
+    pk.x = (uint32_t)res[0] | ((uint32_t)res[1] << 16);
+    pk.y = (uint32_t)res[2] | ((uint32_t)res[3] << 16);
+    *reinterpret_cast<uint2*>(out + ((int64_t)b * QROWS + r) * DIM + 4 * lane) = pk;
+}
+
+}  // namespace kv800
+
+using namespace kv800;
+
+namespace {
+constexpr int64_t MAX_B = 1 << 20;
+constexpr int NX_DEFAULT = 4;   // exact splits per row in kv800_decode
+constexpr float SCALE = 0.12751743074602467f;   // 128^-0.5 * log2(e)
+
+int64_t choose_spb(int64_t B, int64_t nqmax) {
+    if (nqmax <= 0) return 1;
+    // about 8 resident 128-thread CTAs on each of the 148 SMs
+    const int64_t target = 148 * 8;
+    int64_t spb = (nqmax * B + target - 1) / target;
+    return spb < 1 ? 1 : spb;
+}
+
+int check_paged(const kv800_paged* P, const char* who) {
+    if (!P || !P->epool || !P->eoff || !P->N || !P->NQ || P->ebs <= 0 || P->eoff_stride <= 0) {
+        set_error("%s: null Paged record / epool / eoff / N / NQ, or non-positive ebs / eoff_stride", who);
+        return KV800_ERR_ARG;
+    }
+    if (P->win < 0 || P->nsink < 0 || P->nqmax < 0) {
+        set_error("%s: negative win / nsink / nqmax", who);
+        return KV800_ERR_ARG;
+    }
+    if (P->win == 0 && P->nqmax > 0 && (!P->qpool || !P->boff || P->boff_stride <= 0)) {
+        set_error("%s: quantized layer with nqmax > 0 needs qpool and boff", who);
+        return KV800_ERR_ARG;
+    }
+    if (P->win && P->sk && (!P->sv || !P->skoff || !P->svoff)) {
+        set_error("%s: sinks need sk, sv, skoff and svoff", who);
+        return KV800_ERR_ARG;
+    }
+    return KV800_OK;
+}
+}  // namespace
+
+extern "C" int64_t kv800_decode_workspace_size(int64_t B, int64_t nqmax, int64_t win, int64_t spb) {
+    if (B < 0) return -1;
+    const int64_t nq = win ? 0 : nqmax;
+    if (spb <= 0) spb = choose_spb(B, nq);
+    const int64_t ns = nq > 0 ? (nq + spb - 1) / spb : 0;
+    const int64_t slots = ns + NX_DEFAULT;
+    return 256 + B * slots * QROWS * (int64_t)sizeof(float) * (2 + DIM) + 256;
+}
+
+static int launch_decode_parts(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t, const uint16_t* sin_t,
+                               int64_t npos, int64_t B, int64_t ns, int64_t spb, int64_t nx, float* mo, float* lo,
+                               float* ao, int* status, cudaStream_t st, const char* who) {
+    const int nslots = (int)(ns + nx);
+    if (ns > 0) {
+        QArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
+                 mo, lo, ao, nslots, (int)spb, SCALE, status};
+        qdecode_simt<<<dim3((unsigned)B, (unsigned)ns), 128, 0, st>>>(qa);
+        int rc = cuda_status(cudaGetLastError(), who);
+        if (rc) return rc;
+    }
+    XArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, nslots, (int)ns, (int)nx, SCALE, status};
+    xdecode_simt<<<dim3((unsigned)B, (unsigned)nx), 128, 0, st>>>(xa);
+    return cuda_status(cudaGetLastError(), who);
+}
+
+extern "C" int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t, const uint16_t* sin_t,
+                            int64_t npos, int64_t B, int64_t spb, uint16_t* out, void* workspace,
+                            int64_t workspace_bytes, void* stream) {
+    int rc = check_paged(P, "kv800_decode");
+    if (rc) return rc;
+    if (B < 0 || B > MAX_B) {
+        set_error("kv800_decode: batch %lld outside [0, %lld]", (long long)B, (long long)MAX_B);
+        return B < 0 ? KV800_ERR_ARG : KV800_ERR_RANGE;
+    }
+    if (B == 0) return KV800_OK;
+    if (!q || !cos_t || !sin_t || !out || !workspace || npos <= 0) {
+        set_error("kv800_decode: null q / cos / sin / out / workspace or npos <= 0");
+        return KV800_ERR_ARG;
+    }
+    if ((reinterpret_cast<uintptr_t>(cos_t) | reinterpret_cast<uintptr_t>(sin_t)) & 15u) {
+        set_error("kv800_decode: cos / sin tables must be 16-byte aligned");
+        return KV800_ERR_ARG;
+    }
+    if (reinterpret_cast<uintptr_t>(out) & 7u) {
+        set_error("kv800_decode: out must be 8-byte aligned");
+        return KV800_ERR_ARG;
+    }
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) {
+        set_error("kv800_decode: workspace must be 256-byte aligned");
+        return KV800_ERR_ARG;
+    }
+    const int64_t nq = P->win ? 0 : P->nqmax;
+    if (spb <= 0) spb = choose_spb(B, nq);
+    const int64_t ns = nq > 0 ? (nq + spb - 1) / spb : 0;
+    if (ns > 65535) {
+        set_error("kv800_decode: %lld splits above the grid limit (raise spb)", (long long)ns);
+        return KV800_ERR_RANGE;
+    }
+    const int64_t need = kv800_decode_workspace_size(B, P->nqmax, P->win, spb);
+    if (workspace_bytes < need) {
+        set_error("kv800_decode: workspace of %lld bytes, %lld needed", (long long)workspace_bytes, (long long)need);
+        return KV800_ERR_RANGE;
+    }
+    cudaStream_t st = as_stream(stream);
+    char* ws = static_cast<char*>(workspace);
+    int* status = reinterpret_cast<int*>(ws);
+    const int64_t nslots = ns + NX_DEFAULT;
+    float* mo = reinterpret_cast<float*>(ws + 256);
+    float* lo = mo + B * nslots * QROWS;
+    float* ao = lo + B * nslots * QROWS;
+    rc = cuda_status(cudaMemsetAsync(status, 0, sizeof(int), st), "kv800_decode status reset");
+    if (rc) return rc;
+    rc = launch_decode_parts(P, q, cos_t, sin_t, npos, B, ns, spb, NX_DEFAULT, mo, lo, ao, status, st, "kv800_decode");
+    if (rc) return rc;
+    combine_kernel<<<(unsigned)B, 512, 0, st>>>(mo, lo, ao, (int)ns, (int)nslots, out);
+    return cuda_status(cudaGetLastError(), "kv800_decode combine");
+}
+
+extern "C" int kv800_qdecode(const uint16_t* q, const uint8_t* qpool, int64_t qpool_bytes, const int64_t* boff,
+                             int64_t boff_stride, const int32_t* NQ, const uint16_t* cos_t, const uint16_t* sin_t,
+                             int64_t npos, float* mo, float* lo, float* ao, int64_t B, int64_t ns, int64_t spb,
+                             int64_t nqmax, float scale, int* status, void* stream) {
+    if (B < 0 || ns < 0 || spb <= 0) {
+        set_error("kv800_qdecode: negative B / ns or spb <= 0");
+        return KV800_ERR_ARG;
+    }
+    if (B == 0 || ns == 0) return KV800_OK;
+    if (!q || !qpool || !boff || !NQ || !cos_t || !sin_t || !mo || !lo || !ao || boff_stride <= 0) {
+        set_error("kv800_qdecode: null pointer or boff_stride <= 0");
+        return KV800_ERR_ARG;
+    }
+    if ((reinterpret_cast<uintptr_t>(cos_t) | reinterpret_cast<uintptr_t>(sin_t)) & 15u) {
+        set_error("kv800_qdecode: cos / sin tables must be 16-byte aligned");
+        return KV800_ERR_ARG;
+    }
+    if (B > MAX_B || ns > 65535) {
+        set_error("kv800_qdecode: B %lld / ns %lld above the limits", (long long)B, (long long)ns);
+        return KV800_ERR_RANGE;
+    }
+    QArgs qa{q, qpool, qpool_bytes, boff, boff_stride, NQ, nqmax, cos_t, sin_t, npos,
+             mo, lo, ao, (int)(ns + 1), (int)spb, scale, status};
+    qdecode_simt<<<dim3((unsigned)B, (unsigned)ns), 128, 0, as_stream(stream)>>>(qa);
+    return cuda_status(cudaGetLastError(), "kv800_qdecode launch");
+}
+
+extern "C" int kv800_xdecode(const uint16_t* q, const kv800_paged* P, const uint16_t* cos_t, const uint16_t* sin_t,
+                             int64_t npos, float* mo, float* lo, float* ao, int64_t B, int64_t ns, float scale,
+                             int* status, void* stream) {
+    int rc = check_paged(P, "kv800_xdecode");
+    if (rc) return rc;
+    if (B < 0 || ns < 0) {
+        set_error("kv800_xdecode: negative B / ns");
+        return KV800_ERR_ARG;
+    }
+    if (B == 0) return KV800_OK;
+    if (!q || !cos_t || !sin_t || !mo || !lo || !ao) {
+        set_error("kv800_xdecode: null pointer");
+        return KV800_ERR_ARG;
+    }
+    if (reinterpret_cast<uintptr_t>(ao) & 15u) {
+        set_error("kv800_xdecode: ao must be 16-byte aligned");
+        return KV800_ERR_ARG;
+    }
+    if (B > MAX_B) {
+        set_error("kv800_xdecode: B %lld above the limit", (long long)B);
+        return KV800_ERR_RANGE;
+    }
+    XArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, (int)(ns + 1), (int)ns, 1, scale, status};
+    xdecode_simt<<<dim3((unsigned)B, 1), 128, 0, as_stream(stream)>>>(xa);
+    return cuda_status(cudaGetLastError(), "kv800_xdecode launch");
+}
+
+extern "C" int kv800_combine(const float* mo, const float* lo, const float* ao, int64_t B, int64_t ns, uint16_t* out,
+                             void* stream) {
+    if (B < 0 || ns < 0) {
+        set_error("kv800_combine: negative B / ns");
+        return KV800_ERR_ARG;
+    }
+    if (B == 0) return KV800_OK;
+    if (!mo || !lo || !ao || !out) {
+        set_error("kv800_combine: null pointer");
+        return KV800_ERR_ARG;
+    }
+    if ((reinterpret_cast<uintptr_t>(ao) & 15u) || (reinterpret_cast<uintptr_t>(out) & 7u)) {
+        set_error("kv800_combine: ao must be 16-byte and out 8-byte aligned");
+        return KV800_ERR_ARG;
+    }
+    combine_kernel<<<(unsigned)B, 512, 0, as_stream(stream)>>>(mo, lo, ao, (int)ns, (int)(ns + 1), out);
+    return cuda_status(cudaGetLastError(), "kv800_combine launch");
+}

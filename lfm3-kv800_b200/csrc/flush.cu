@@ -1,0 +1,428 @@
+// 800h quantizer / flush on sm_100a: packs 256-token sub-blocks of bf16 K / V into the 51,200-byte layout, bit-exact
+// with the reference torch quantizer (lfm3_kv800/kv800.py:56-76), plus the exact-page scatter of new tokens
+// (kv800.py:423-428, vllm_attn.py:261-269).
+//
+// One launch covers M sub-blocks with grid (M, 1 + VSPLIT):
+//   blockIdx.y == 0        K part: 4 heads x 128 channels; lo / hi over the 256 tokens per channel, fp8 lo and
+//                          scale (hi - lo) / 3, 2-bit codes (IEEE divide, round half to even), planar bytes.
+//   blockIdx.y == 1..4     V part for 64 tokens: y = v @ H per head as the sequential fp32 FMA chain over i that the
+//                          reference's CPU BLAS computes (bit-exact requirement), lo / hi per (token, 2-head group),
+//                          1-bit codes, planar bytes.
+// The V part is the arithmetic bound of the kernel (128 FMA per output element, 16.8 M FMA per sub-block); the K part
+// streams 256 KB per sub-block twice (the second pass is served by L2).
+#include <cstdarg>
+#include <cstdio>
+
+#include "kv800_common.cuh"
+
+namespace kv800 {
+
+// Where the 256 x 4 K / V rows of sub-block m come from and where its 51,200 bytes go.
+struct ContigSrc {
+    const uint16_t* k;
+    const uint16_t* v;
+    uint8_t* out;
+    __device__ __forceinline__ bool rows(int64_t m, int t, int h, const uint16_t*& kr, const uint16_t*& vr) const {
+        int64_t o = ((m * BLK + t) * HEADS + h) * DIM;
+        kr = k + o;
+        vr = v + o;
+        return true;
+    }
+    __device__ __forceinline__ uint8_t* dst(int64_t m) const { return out + m * SUB; }
+};
+
+struct PagedSrc {
+    const uint16_t* epool;
+    int64_t epool_elems;
+    const int64_t* eoff;
+    int64_t eoff_stride, ebs, e_hs, e_ts, e_v;
+    uint8_t* qpool;
+    int64_t qpool_bytes;
+    const int64_t* boff;
+    int64_t boff_stride;
+    const int32_t* seq;
+    const int32_t* blk;
+    int64_t nseq;
+    int* status;
+    __device__ __forceinline__ bool rows(int64_t m, int t, int h, const uint16_t*& kr, const uint16_t*& vr) const {
+        int64_t b = seq[m], j = blk[m];
+        int64_t p = j * BLK + t;
+        if (b < 0 || b >= nseq || j < 0 || p / ebs >= eoff_stride) {
+            flag(status, ST_TABLE);
+            return false;
+        }
+        int64_t o = eoff[b * eoff_stride + p / ebs] + h * e_hs + (p % ebs) * e_ts;
+        if (o < 0 || o + DIM > epool_elems || o + e_v < 0 || o + e_v + DIM > epool_elems) {
+            flag(status, ST_EPOOL);
+            return false;
+        }
+        kr = epool + o;
+        vr = epool + o + e_v;
+        return true;
+    }
+    __device__ __forceinline__ uint8_t* dst(int64_t m) const {
+        int64_t b = seq[m], j = blk[m];
+        if (b < 0 || b >= nseq || j < 0 || j >= boff_stride) {
+            flag(status, ST_TABLE);
+            return nullptr;
+        }
+        int64_t o = boff[b * boff_stride + j];
+        if (o < 0 || o + SUB > qpool_bytes) {
+            flag(status, ST_QPOOL);
+            return nullptr;
+        }
+        return qpool + o;
+    }
+};
+
+constexpr int VSPLIT = 4;               // V-part CTAs per sub-block (64 tokens each)
+constexpr int VTOK = BLK / VSPLIT;
+
+// 16 bf16 of a row at element offset e (e a multiple of 16), as fp32; vector loads when the row is 16-byte aligned.
+__device__ __forceinline__ void load16(const uint16_t* row, int e, float* out) {
+    const uint16_t* p = row + e;
+    if ((reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
+        uint4 a = *reinterpret_cast<const uint4*>(p);
+        uint4 b = *reinterpret_cast<const uint4*>(p + 8);
+        uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            out[2 * i] = __uint_as_float(w[i] << 16);
+            out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; i++) out[i] = bf2f(p[i]);
+    }
+}
+
+
+// y[h][k] = (x_h @ H)[lane + 32 k] for the 4 rows x_h = rows[h * 128 .. h * 128 + 127] (fp32, shared memory), each
+// output the sequential chain acc = fma(x_i, H[i][d], acc), i = 0 .. 127, from acc = 0: the arithmetic of the
+// reference's CPU BLAS for v.float() @ H, so the result is bit-identical.  C[b] = +-c for the lane part of the sign
+// (parity(b & lane)); the (a, k) part of the sign, parity(a & k) for i = 32 a + b and d = lane + 32 k, is folded
+// into the operand at compile time.
+__device__ __forceinline__ void hadamard_rows(const float* rows, const float (&C)[32], float (&y)[HEADS][4]) {
+#pragma unroll
+    for (int hp = 0; hp < 2; hp++) {
+        float acc[2][4];
+#pragma unroll
+        for (int q = 0; q < 2; q++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) acc[q][k] = 0.f;
+        const float* v0 = rows + (2 * hp) * DIM;
+        const float* v1 = rows + (2 * hp + 1) * DIM;
+#pragma unroll
+        for (int a = 0; a < 4; a++) {
+#pragma unroll
+            for (int b4 = 0; b4 < 32; b4 += 4) {
+                float4 x0 = *reinterpret_cast<const float4*>(v0 + 32 * a + b4);
+                float4 x1 = *reinterpret_cast<const float4*>(v1 + 32 * a + b4);
+                float xs0[4] = {x0.x, x0.y, x0.z, x0.w}, xs1[4] = {x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const bool neg = (__builtin_popcount(a & k) & 1) != 0;
+                        acc[0][k] = fmaf(neg ? -xs0[u] : xs0[u], C[b4 + u], acc[0][k]);
+                        acc[1][k] = fmaf(neg ? -xs1[u] : xs1[u], C[b4 + u], acc[1][k]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            y[2 * hp][k] = acc[0][k];
+            y[2 * hp + 1][k] = acc[1][k];
+        }
+    }
+}
+
+__device__ __forceinline__ void hadamard_signs(int lane, float (&C)[32]) {
+    const float c = 0.0883883461356163f;   // fp32(1 / sqrt(128)), the entry magnitude of the reference's hadamard()
+#pragma unroll
+    for (int b = 0; b < 32; b++) C[b] = (__popc(b & lane) & 1) ? -c : c;
+}
+
+template <class Src>
+__global__ void __launch_bounds__(256) flush_kernel(Src src) {
+    const int64_t m = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint8_t* out = src.dst(m);
+    if (out == nullptr) return;
+
+    if (blockIdx.y == 0) {
+        // ---------------- K part. thread = (token half, head, j); channels j, j+32, j+64, j+96 of head h.
+        __shared__ float slo[2][HEADS][DIM], shi[2][HEADS][DIM];
+        const int half = tid >> 7, h = (tid >> 5) & 3, j = lane;
+        float lo[4], hi[4];
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            lo[p] = __int_as_float(0x7f800000);
+            hi[p] = -__int_as_float(0x7f800000);
+        }
+        for (int t = half * 128; t < half * 128 + 128; t++) {
+            const uint16_t *kr, *vr;
+            float x[4] = {0.f, 0.f, 0.f, 0.f};
+            if (src.rows(m, t, h, kr, vr)) {
+#pragma unroll
+                for (int p = 0; p < 4; p++) x[p] = bf2f(kr[j + 32 * p]);
+            }
+#pragma unroll
+            for (int p = 0; p < 4; p++) {
+                lo[p] = fminf(lo[p], x[p]);
+                hi[p] = fmaxf(hi[p], x[p]);
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            slo[half][h][j + 32 * p] = lo[p];
+            shi[half][h][j + 32 * p] = hi[p];
+        }
+        __syncthreads();
+        float lof[4], scf[4];
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            const int c = j + 32 * p;
+            float l = fminf(slo[0][h][c], slo[1][h][c]), u = fmaxf(shi[0][h][c], shi[1][h][c]);
+            uint32_t lo8 = f8enc(l);
+            uint32_t sc8 = f8enc(clamp_min_1e8(__fdiv_rn(u - l, 3.0f)));
+            lof[p] = f8dec(lo8);
+            scf[p] = clamp_min_1e8(f8dec(sc8));
+            if (half == 0) {
+                out[KLO_O + h * DIM + c] = (uint8_t)lo8;
+                out[KSC_O + h * DIM + c] = (uint8_t)sc8;
+            }
+        }
+        for (int t = half * 128; t < half * 128 + 128; t++) {
+            const uint16_t *kr, *vr;
+            float x[4] = {0.f, 0.f, 0.f, 0.f};
+            if (src.rows(m, t, h, kr, vr)) {
+#pragma unroll
+                for (int p = 0; p < 4; p++) x[p] = bf2f(kr[j + 32 * p]);
+            }
+            uint32_t byte = 0;
+#pragma unroll
+            for (int p = 0; p < 4; p++) byte |= round_clamp(__fdiv_rn(x[p] - lof[p], scf[p]), 3.0f) << (2 * p);
+            out[KC_O + (t * HEADS + h) * 32 + j] = (uint8_t)byte;
+        }
+        return;
+    }
+
+    // ---------------- V part: warp w handles tokens t0 + w, t0 + w + 8, ... of this CTA's 64-token slice.
+    __shared__ float vbuf[8][HEADS * DIM];
+    float C[32];
+    hadamard_signs(lane, C);
+    const int t0 = (blockIdx.y - 1) * VTOK;
+    for (int tt = warp; tt < VTOK; tt += 8) {
+        const int t = t0 + tt;
+        // stage the 4 V rows (512 values) of token t as fp32: lane loads 16 values of head lane / 8
+        {
+            const int h = lane >> 3, e = (lane & 7) * 16;
+            const uint16_t *kr, *vr;
+            float x[16];
+            if (src.rows(m, t, h, kr, vr)) load16(vr, e, x);
+            else
+#pragma unroll
+                for (int i = 0; i < 16; i++) x[i] = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; i++) vbuf[warp][h * DIM + e + i] = x[i];
+        }
+        __syncwarp();
+        float y[HEADS][4];
+        hadamard_rows(vbuf[warp], C, y);
+        __syncwarp();
+        // per 2-head group: lo / hi over 256 dims, fp8 lo and scale hi - lo, 1-bit codes
+        uint32_t part[HEADS];
+#pragma unroll
+        for (int h = 0; h < HEADS; h++) part[h] = 0;
+#pragma unroll
+        for (int g = 0; g < 2; g++) {
+            float l = y[2 * g][0], u = y[2 * g][0];
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    l = fminf(l, y[2 * g + hh][k]);
+                    u = fmaxf(u, y[2 * g + hh][k]);
+                }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                l = fminf(l, __shfl_xor_sync(0xffffffffu, l, o));
+                u = fmaxf(u, __shfl_xor_sync(0xffffffffu, u, o));
+            }
+            uint32_t lo8 = f8enc(l), sc8 = f8enc(clamp_min_1e8(u - l));
+            float lof = f8dec(lo8), scf = clamp_min_1e8(f8dec(sc8));
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++)
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                    part[2 * g + hh] |= round_clamp(__fdiv_rn(y[2 * g + hh][k] - lof, scf), 1.0f)
+                                        << ((lane >> 4) + 2 * k);
+            if (lane == 0) {
+                out[VLO_O + t * 2 + g] = (uint8_t)lo8;
+                out[VSC_O + t * 2 + g] = (uint8_t)sc8;
+            }
+        }
+        // byte j of (t, h) holds dims j + 16 i at bit i; lane (j, half) owns i = half + 2k
+#pragma unroll
+        for (int h = 0; h < HEADS; h++) {
+            uint32_t byte = part[h] | __shfl_xor_sync(0xffffffffu, part[h], 16);
+            if (lane < 16) out[VB_O + (t * HEADS + h) * 16 + lane] = (uint8_t)byte;
+        }
+    }
+}
+
+
+// Dequantizer (kv800.py:79-92): K (M, 256, 4, 128) bf16 = bf16(codes * ksc + klo) (exact in fp32, then rounded);
+// V (M, 256, 4, 128) fp32 = (bits * vsc + vlo) @ H with the same FMA chain as the quantizer (bit-identical to the
+// reference on CPU).  grid (M, 8): 32 tokens per CTA, warp = 4 tokens.
+__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* sb_all, uint16_t* kout, float* vout) {
+    const int64_t m = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint8_t* sb = sb_all + m * SUB;
+    __shared__ float vbuf[8][HEADS * DIM];
+    float C[32];
+    hadamard_signs(lane, C);
+    for (int tt = 0; tt < 4; tt++) {
+        const int t = blockIdx.y * 32 + warp * 4 + tt;
+        // K: lane covers channel j = lane of each plane for the 4 heads
+#pragma unroll
+        for (int h = 0; h < HEADS; h++) {
+            const uint32_t byte = sb[KC_O + (t * HEADS + h) * 32 + lane];
+#pragma unroll
+            for (int p = 0; p < 4; p++) {
+                const int d = lane + 32 * p;
+                const float sc = f8dec(sb[KSC_O + h * DIM + d]), lo = f8dec(sb[KLO_O + h * DIM + d]);
+                const float code = (float)((byte >> (2 * p)) & 3u);
+                kout[((m * BLK + t) * HEADS + h) * DIM + d] = f2bf(code * sc + lo);
+            }
+        }
+        // V in the Hadamard domain: y_d = bit_d * vsc + vlo, then rotated
+#pragma unroll
+        for (int h = 0; h < HEADS; h++) {
+            const float vlo = f8dec(sb[VLO_O + t * 2 + (h >> 1)]), vsc = f8dec(sb[VSC_O + t * 2 + (h >> 1)]);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int d = lane + 32 * k;
+                const uint32_t bit = (sb[VB_O + (t * HEADS + h) * 16 + (d & 15)] >> (d >> 4)) & 1u;
+                vbuf[warp][h * DIM + d] = (float)bit * vsc + vlo;
+            }
+        }
+        __syncwarp();
+        float y[HEADS][4];
+        hadamard_rows(vbuf[warp], C, y);
+#pragma unroll
+        for (int h = 0; h < HEADS; h++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) vout[((m * BLK + t) * HEADS + h) * DIM + lane + 32 * k] = y[h][k];
+        __syncwarp();
+    }
+}
+
+// Exact-page scatter: one warp per (token, head, K|V) row of 128 bf16 (256 B, 8 B per lane).
+__global__ void write_exact_kernel(uint16_t* epool, int64_t epool_elems, const int64_t* eoff, int64_t eoff_stride,
+                                   int64_t ebs, int64_t e_hs, int64_t e_ts, int64_t e_v, const uint16_t* k,
+                                   const uint16_t* v, const int32_t* seq, const int64_t* pos, int64_t T, int64_t nseq,
+                                   int* status) {
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= T * HEADS * 2) return;
+    const int64_t i = row / (HEADS * 2);
+    const int h = (int)((row / 2) % HEADS), isv = (int)(row & 1);
+    const int64_t b = seq[i], p = pos[i];
+    if (b < 0 || b >= nseq || p < 0 || p / ebs >= eoff_stride) {
+        if (lane == 0) flag(status, ST_TABLE);
+        return;
+    }
+    const int64_t o = eoff[b * eoff_stride + p / ebs] + h * e_hs + (p % ebs) * e_ts + (isv ? e_v : 0);
+    if (o < 0 || o + DIM > epool_elems) {
+        if (lane == 0) flag(status, ST_EPOOL);
+        return;
+    }
+    const uint16_t* srow = (isv ? v : k) + (i * HEADS + h) * DIM;
+    uint16_t* drow = epool + o;
+#pragma unroll
+    for (int e = 0; e < 4; e++) drow[lane * 4 + e] = srow[lane * 4 + e];
+}
+
+}  // namespace kv800
+
+using namespace kv800;
+
+extern "C" int kv800_quantize_blocks(const uint16_t* k, const uint16_t* v, int64_t M, uint8_t* out, void* stream) {
+    if (M < 0 || (M > 0 && (!k || !v || !out))) {
+        set_error("kv800_quantize_blocks: null pointer or negative M (%lld)", (long long)M);
+        return KV800_ERR_ARG;
+    }
+    if (M == 0) return KV800_OK;
+    if (M > 0x7fffffffLL) {
+        set_error("kv800_quantize_blocks: M = %lld above 2^31 - 1", (long long)M);
+        return KV800_ERR_RANGE;
+    }
+    ContigSrc s{k, v, out};
+    flush_kernel<ContigSrc><<<dim3((unsigned)M, 1 + VSPLIT), 256, 0, as_stream(stream)>>>(s);
+    return cuda_status(cudaGetLastError(), "kv800_quantize_blocks launch");
+}
+
+extern "C" int kv800_flush(const uint16_t* epool, int64_t epool_elems, const int64_t* eoff, int64_t eoff_stride,
+                           int64_t ebs, int64_t e_hs, int64_t e_ts, int64_t e_v, uint8_t* qpool, int64_t qpool_bytes,
+                           const int64_t* boff, int64_t boff_stride, const int32_t* seq, const int32_t* blk,
+                           int64_t M, int64_t nseq, int* status, void* stream) {
+    if (M < 0 || nseq < 0) {
+        set_error("kv800_flush: negative M (%lld) or nseq (%lld)", (long long)M, (long long)nseq);
+        return KV800_ERR_ARG;
+    }
+    if (M == 0) return KV800_OK;
+    if (!epool || !eoff || !qpool || !boff || !seq || !blk || ebs <= 0 || eoff_stride <= 0 || boff_stride <= 0) {
+        set_error("kv800_flush: null pointer or non-positive ebs / stride");
+        return KV800_ERR_ARG;
+    }
+    if (M > 0x7fffffffLL) {
+        set_error("kv800_flush: M = %lld above 2^31 - 1", (long long)M);
+        return KV800_ERR_RANGE;
+    }
+    PagedSrc s{epool, epool_elems, eoff, eoff_stride, ebs, e_hs, e_ts, e_v, qpool, qpool_bytes,
+               boff, boff_stride, seq, blk, nseq, status};
+    flush_kernel<PagedSrc><<<dim3((unsigned)M, 1 + VSPLIT), 256, 0, as_stream(stream)>>>(s);
+    return cuda_status(cudaGetLastError(), "kv800_flush launch");
+}
+
+extern "C" int kv800_write_exact(uint16_t* epool, int64_t epool_elems, const int64_t* eoff, int64_t eoff_stride,
+                                 int64_t ebs, int64_t e_hs, int64_t e_ts, int64_t e_v, const uint16_t* k,
+                                 const uint16_t* v, const int32_t* seq, const int64_t* pos, int64_t T, int64_t nseq,
+                                 int* status, void* stream) {
+    if (T < 0) {
+        set_error("kv800_write_exact: negative T (%lld)", (long long)T);
+        return KV800_ERR_ARG;
+    }
+    if (T == 0) return KV800_OK;
+    if (!epool || !eoff || !k || !v || !seq || !pos || ebs <= 0 || eoff_stride <= 0) {
+        set_error("kv800_write_exact: null pointer or non-positive ebs / stride");
+        return KV800_ERR_ARG;
+    }
+    const int64_t rows = T * HEADS * 2, per = 8;   // 8 warps per block
+    const int64_t blocks = (rows + per - 1) / per;
+    if (blocks > 0x7fffffffLL) {
+        set_error("kv800_write_exact: T = %lld too large", (long long)T);
+        return KV800_ERR_RANGE;
+    }
+    write_exact_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(epool, epool_elems, eoff, eoff_stride, ebs,
+                                                                       e_hs, e_ts, e_v, k, v, seq, pos, T, nseq,
+                                                                       status);
+    return cuda_status(cudaGetLastError(), "kv800_write_exact launch");
+}
+
+extern "C" int kv800_dequantize_blocks(const uint8_t* sb, int64_t M, uint16_t* k_out, float* v_out, void* stream) {
+    if (M < 0 || (M > 0 && (!sb || !k_out || !v_out))) {
+        set_error("kv800_dequantize_blocks: null pointer or negative M (%lld)", (long long)M);
+        return KV800_ERR_ARG;
+    }
+    if (M == 0) return KV800_OK;
+    if (M > 0x7fffffffLL) {
+        set_error("kv800_dequantize_blocks: M = %lld above 2^31 - 1", (long long)M);
+        return KV800_ERR_RANGE;
+    }
+    dequant_kernel<<<dim3((unsigned)M, 8), 256, 0, as_stream(stream)>>>(sb, k_out, v_out);
+    return cuda_status(cudaGetLastError(), "kv800_dequantize_blocks launch");
+}

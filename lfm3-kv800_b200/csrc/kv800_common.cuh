@@ -1,0 +1,76 @@
+// Shared device helpers of the 800h CUDA library (sm_100a): layout constants, bf16 / fp8 e4m3fn conversions written
+// from the format definitions, the device status word, and the host-side error plumbing of the C ABI.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/kv800_b200.h"
+
+namespace kv800 {
+
+// Sub-block byte map (lfm3_kv800/kv800.py:3-10,32-34).
+constexpr int BLK = 256, LAG = 128, NSINK = 4, WIN = 256;
+constexpr int SUB = 51200;
+constexpr int KC_O = 0, VB_O = 32768, VLO_O = 49152, VSC_O = 49664, KLO_O = 50176, KSC_O = 50688;
+constexpr int HEADS = 4, DIM = 128, QROWS = 16;
+
+// Status bits written by the device-side range checks (first event wins for the index fields).
+constexpr int ST_QPOOL = 1, ST_EPOOL = 2, ST_SINK = 4, ST_TABLE = 8, ST_TIMEOUT = 16;
+
+__device__ __forceinline__ void flag(int* status, int bit) {
+    if (status) atomicOr(status, bit);
+}
+
+__device__ __forceinline__ float bf2f(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
+
+// fp32 -> bf16 bits, round to nearest even (NaN kept quiet).
+__device__ __forceinline__ uint16_t f2bf(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+__device__ __forceinline__ float bfround(float f) { return bf2f(f2bf(f)); }
+
+// fp8 e4m3fn byte -> fp32, exact (bias 7, 3 mantissa bits; e = 0 is the subnormal grid m * 2^-9; 0x7f / 0xff NaN).
+__device__ __forceinline__ float f8dec(uint32_t b) {
+    uint32_t e = (b >> 3) & 15u, m = b & 7u;
+    float mag = e ? __uint_as_float(((e + 120u) << 23) | (m << 20)) : (float)m * 0.001953125f;
+    if (e == 15u && m == 7u) mag = __uint_as_float(0x7fc00000u);
+    return (b & 0x80u) ? -mag : mag;
+}
+
+// fp32 -> fp8 e4m3fn byte with the semantics of torch's non-saturating cast: round to nearest even, magnitudes above
+// 464 (those that would round past 448), infinities and NaN -> 0x7f with the sign kept.  Written from the format
+// definition: subnormals are the integer multiples of 2^-9 below 2^-6 (exact scaling then RNE), normals round the
+// fp32 mantissa to 3 bits with a carry into the exponent.
+__device__ __forceinline__ uint32_t f8enc(float f) {
+    uint32_t u = __float_as_uint(f);
+    uint32_t sign = (u >> 24) & 0x80u;
+    uint32_t a = u & 0x7fffffffu;
+    float af = __uint_as_float(a);
+    if (a > 0x7f800000u || !(af <= 464.0f)) return sign | 0x7fu;
+    if (af < 0.015625f) return sign | (uint32_t)__float2int_rn(af * 512.0f);
+    uint32_t r = a + 0x7ffffu + ((a >> 20) & 1u);
+    uint32_t e = (r >> 23) - 120u;
+    return sign | (e << 3) | ((r >> 20) & 7u);
+}
+
+// torch clamp_min(x, 1e-8): NaN propagates.
+__device__ __forceinline__ float clamp_min_1e8(float x) { return (x != x) ? x : fmaxf(x, 1e-8f); }
+
+// torch .round().clamp(0, hi).to(uint8) of an fp32 value: half to even, NaN -> 0.
+__device__ __forceinline__ uint32_t round_clamp(float x, float hi) {
+    if (x != x) return 0u;
+    float r = fminf(fmaxf(rintf(x), 0.0f), hi);
+    return (uint32_t)r;
+}
+
+}  // namespace kv800
+
+// ------------------------------------------------------------------ host side of the C ABI
+namespace kv800 {
+void set_error(const char* fmt, ...);
+int cuda_status(cudaError_t e, const char* what);
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+}  // namespace kv800

@@ -1,0 +1,72 @@
+"""The C-ABI library without a GPU: it loads, exports every entry point include/kv800_b200.h declares, and rejects
+bad arguments on the host before any launch (no kernel runs in these tests)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from lfm3_kv800 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "kv800_b200.h")
+
+
+def declared():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"KV800_API\s+[\w\s\*]+?\b(kv800_\w+)\s*\(", src)))
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    for n in ("kv800_quantize_blocks", "kv800_dequantize_blocks", "kv800_flush", "kv800_write_exact", "kv800_decode",
+              "kv800_qdecode", "kv800_xdecode", "kv800_combine"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.lib()
+    for n in declared():
+        assert hasattr(L, n), n
+    assert set(declared()) <= set(_lib.SIGNATURES), "a declared entry point has no ctypes signature"
+
+
+def test_abi_and_constants():
+    L = _lib.lib()
+    assert L.kv800_abi_version() == 1
+    v = [ctypes.c_int64() for _ in range(5)]
+    assert L.kv800_constants(*[ctypes.byref(x) for x in v]) == 0
+    assert [x.value for x in v] == [256, 51200, 128, 4, 256]
+
+
+def test_struct_layout_matches_header():
+    # 23 eight-byte fields in the order of struct kv800_paged
+    assert ctypes.sizeof(_lib.Paged) == 23 * 8
+    src = open(HEADER).read()
+    body = src[src.index("typedef struct kv800_paged"):src.index("} kv800_paged;")]
+    fields = re.findall(r"\*?\s*(\w+)\s*[;,]", body.split("{", 1)[1])
+    assert [f for f, _ in _lib.Paged._fields_] == fields
+
+
+def test_host_argument_checks():
+    L = _lib.lib()
+    assert L.kv800_quantize_blocks(None, None, -1, None, None) == _lib.ERR_ARG
+    assert b"negative" in L.kv800_last_error()
+    assert L.kv800_quantize_blocks(None, None, 0, None, None) == _lib.OK          # empty: nothing to do
+    assert L.kv800_quantize_blocks(None, None, 4, None, None) == _lib.ERR_ARG
+    assert L.kv800_flush(None, 0, None, 1, 64, 0, 0, 0, None, 0, None, 1, None, None, -3, 1, None, None) == _lib.ERR_ARG
+    assert L.kv800_decode(None, None, None, None, 1, 1, 0, None, None, 0, None) == _lib.ERR_ARG
+    assert b"Paged" in L.kv800_last_error()
+    P = _lib.Paged()
+    assert L.kv800_decode(ctypes.byref(P), None, None, None, 1, 1, 0, None, None, 0, None) == _lib.ERR_ARG
+    assert L.kv800_check_status(None, None, None) == _lib.ERR_ARG
+
+
+@pytest.mark.parametrize("B,nqmax,win", [(64, 127, 0), (4, 7, 0), (64, 0, 256), (2048, 127, 0)])
+def test_workspace_size(B, nqmax, win):
+    L = _lib.lib()
+    ws = L.kv800_decode_workspace_size(B, nqmax, win, 0)
+    assert ws >= 256 + B * 16 * 130 * 4 * 4
+    spb = max(1, -(-nqmax * B // (148 * 8))) if (nqmax and not win) else 1
+    ns = -(-nqmax // spb) if (nqmax and not win) else 0
+    assert ws == 256 + B * (ns + 4) * 16 * 4 * 130 + 256

@@ -1,0 +1,78 @@
+"""Host-side logic of the package without a GPU: the backend surface keeps the reference's names and error
+behaviour (kv800.py:251-349) with a single 'cuda' backend, and nothing silently runs on the CPU."""
+import numpy as np
+import pytest
+import torch
+
+from lfm3_kv800 import kv800
+from oracle import oracle as O
+
+
+def test_constants_match_reference_layout():
+    assert (kv800.BLK, kv800.LAG, kv800.NSINK, kv800.WIN, kv800.SUB) == (256, 128, 4, 256, 51200)
+    assert (kv800.KC_O, kv800.VB_O, kv800.VLO_O, kv800.VSC_O, kv800.KLO_O, kv800.KSC_O) == (
+        0, 32768, 49152, 49664, 50176, 50688)
+    assert kv800.F8 is torch.float8_e4m3fn
+    assert kv800.BACKENDS == ("cuda",)
+
+
+def test_hadamard_and_flat():
+    H = kv800.hadamard(128)
+    np.testing.assert_array_equal(H.numpy(), O.hadamard(128))
+    assert torch.allclose(H @ H.T, torch.eye(128), atol=1e-6)
+    base = torch.arange(100, dtype=torch.float32)
+    v = base[10:20]
+    f = kv800.flat(v)
+    assert f.shape == (90,) and f[0] == 10 and f.data_ptr() == v.data_ptr()
+
+
+def test_backend_selection_names():
+    try:
+        kv800.set_backend("cuda")
+        kv800.set_backend("auto")
+        kv800.set_backend(None)
+        for bad in ("triton", "sycl", "torch", "nope"):
+            with pytest.raises(ValueError):
+                kv800.set_backend(bad)
+    finally:
+        kv800.set_backend(None)
+    ok, why = kv800._available("cuda", "cpu")
+    assert not ok and "cuda devices only" in why
+    ok, why = kv800._available("triton", "cuda")
+    assert not ok
+
+
+def test_env_backend(monkeypatch):
+    monkeypatch.setenv("LFM3KV_BACKEND", "triton")
+    with pytest.raises(ValueError):          # set_backend(None) re-reads the env, as in the reference
+        kv800.set_backend(None)
+    with pytest.raises(ValueError):
+        kv800._requested()
+    monkeypatch.setenv("LFM3KV_BACKEND", "cuda")
+    assert kv800._requested() == "cuda"
+
+
+def test_no_cpu_path():
+    """Every product entry point refuses CPU tensors instead of computing on the host."""
+    k = torch.zeros(1, 256, 4, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        kv800.quantize_blocks(k, k, kv800.hadamard())
+    with pytest.raises(RuntimeError, match="CUDA"):
+        kv800.dequantize_blocks(torch.zeros(1, 51200, dtype=torch.uint8))
+    with pytest.raises(RuntimeError, match="cuda"):
+        kv800.PagedStore(1, 300, "cpu")
+    P = kv800.Paged(qpool=torch.zeros(1, 51200, dtype=torch.uint8), boff=torch.zeros(1, 1, dtype=torch.int64),
+                    epool=torch.zeros(10, 4, 64, 256, dtype=torch.bfloat16), eoff=torch.zeros(1, 8, dtype=torch.int64),
+                    ebs=64, e_hs=64 * 256, e_ts=256, e_v=128, N=torch.ones(1, dtype=torch.int32),
+                    NQ=torch.zeros(1, dtype=torch.int32), nqmax=0, win=0)
+    q = torch.zeros(1, 16, 128, dtype=torch.bfloat16)
+    cs = torch.ones(16, 32, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        kv800.decode(P, q, cs, cs, kv800.hadamard())
+
+
+def test_paged_slots():
+    P = kv800.Paged(win=256, nqmax=3)
+    assert P.win == 256 and P.nqmax == 3 and P.sk is None
+    assert set(kv800.Paged.__slots__) == {"qpool", "boff", "epool", "eoff", "ebs", "e_hs", "e_ts", "e_v", "sk", "sv",
+                                          "skoff", "svoff", "N", "NQ", "nqmax", "win"}

@@ -1,0 +1,116 @@
+"""The CUDA quantizer / flush / dequantizer against the reference (golden fixtures made from the reference package)
+and the CPU oracle: packed bytes bit-exact, dequantized K bit-exact, dequantized V bit-exact (the same FMA chain)."""
+import numpy as np
+import pytest
+import torch
+
+import inputs as I
+from _util import nb, tb
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+QG = np.load(I.__file__.replace("inputs.py", "quant.npz"))
+DG = np.load(I.__file__.replace("inputs.py", "decode.npz"))
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def kv800():
+    from lfm3_kv800 import kv800 as m
+    return m
+
+
+@pytest.mark.parametrize("kind", I.QUANT_KINDS)
+def test_quantize_blocks_matches_reference(kv800, kind):
+    M = int(QG[f"{kind}_M"])
+    k, v = I.quant_inputs(kind, M)
+    out = kv800.quantize_blocks(tb(k, DEV), tb(v, DEV), kv800.hadamard(128, DEV)).cpu().numpy()
+    if f"{kind}_bytes" in QG:
+        ref = QG[f"{kind}_bytes"]
+        bad = np.nonzero(out != ref)
+        assert bad[0].size == 0, f"{bad[0].size} bytes differ, first at {bad[1][:8]}"
+    assert [I.digest(out[m]) for m in range(M)] == list(QG[f"{kind}_sha"])
+
+
+@pytest.mark.parametrize("kind,M", [("outlier", 37), ("wide", 9), ("normal", 64)])
+def test_quantize_blocks_matches_oracle_many(kv800, kind, M):
+    k, v = I.quant_inputs(kind, M, seed=5)
+    out = kv800.quantize_blocks(tb(k, DEV), tb(v, DEV)).cpu().numpy()
+    np.testing.assert_array_equal(out, O.quantize_blocks(k, v))
+
+
+def test_dequantize_blocks_matches_reference(kv800):
+    kd, vd = kv800.dequantize_blocks(torch.from_numpy(QG["outlier_bytes"]).to(DEV))
+    assert I.digest(nb(kd)) == str(QG["outlier_deq_k_sha"])
+    assert I.digest(vd.cpu().numpy()) == str(QG["outlier_deq_v_sha"])
+
+
+def test_round_trip_idempotent(kv800):
+    """quantize(dequantize(quantize(x))) keeps K codes of the dequantized keys: a size-independent property."""
+    k, v = I.quant_inputs("normal", 8, seed=11)
+    sb = kv800.quantize_blocks(tb(k, DEV), tb(v, DEV))
+    kd, _ = kv800.dequantize_blocks(sb)
+    sb2 = kv800.quantize_blocks(kd.contiguous(), tb(v, DEV))
+    np.testing.assert_array_equal(sb2[:, :32768].cpu().numpy(), sb[:, :32768].cpu().numpy())
+
+
+def _cuda_store(kv800, win, n, B=2):
+    K, V, q = I.parity_inputs(win, n, B=B)
+    st = kv800.PagedStore(B, n + 8, DEV, window=win)
+    pre = max(1, n - 5)
+    st.append(tb(K[:, :pre], DEV), tb(V[:, :pre], DEV))
+    for i in range(pre, n):
+        st.append(tb(K[:, i:i + 1], DEV), tb(V[:, i:i + 1], DEV))
+    return st
+
+
+@pytest.mark.parametrize("win,n", [c for c in I.parity_cases() if c[0] == 0])
+def test_paged_flush_matches_reference(kv800, win, n):
+    """PagedStore.append (CUDA page scatter + flush) gives the reference's pools byte for byte."""
+    st = _cuda_store(kv800, win, n)
+    key = f"w{win}_n{n}"
+    assert st.nq == int(DG[f"{key}_nq"])
+    assert I.digest(st.qpool.cpu().numpy()) == str(DG[f"{key}_qpool_sha"])
+    assert I.digest(nb(st.epool)) == str(DG[f"{key}_epool_sha"])
+
+
+def test_flush_scattered_tables(kv800):
+    """Flush through shuffled page / sub-block tables, many sequences at once, against the oracle."""
+    g = np.random.RandomState(3)
+    B, nsub, ebs = 6, 3, 64
+    npg = nsub * 256 // ebs
+    K = I.f32_to_bf16(g.standard_normal((B, nsub * 256, 4, 128)).astype(np.float32) * 2)
+    V = I.f32_to_bf16(g.standard_normal((B, nsub * 256, 4, 128)).astype(np.float32))
+    pages = g.permutation(B * npg + 5)[:B * npg].reshape(B, npg)
+    epool = np.zeros((B * npg + 5, 4, ebs, 256), np.uint16)
+    for b in range(B):
+        for p in range(nsub * 256):
+            epool[pages[b, p // ebs], :, p % ebs, :128] = K[b, p]
+            epool[pages[b, p // ebs], :, p % ebs, 128:] = V[b, p]
+    eoff = (pages * 4 * ebs * 256).astype(np.int64)
+    boff = (g.permutation(B * nsub + 2)[:B * nsub].reshape(B, nsub) * 51200).astype(np.int64)
+    seq = np.repeat(np.arange(B), nsub).astype(np.int32)
+    blk = np.tile(np.arange(nsub), B).astype(np.int32)
+    qref = np.zeros((B * nsub + 2, 51200), np.uint8)
+    O.flush(epool, eoff, ebs, ebs * 256, 256, 128, qref, boff, seq, blk)
+    qp = torch.zeros(B * nsub + 2, 51200, dtype=torch.uint8, device=DEV)
+    ep = tb(epool, DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    kv800.flush(ep, torch.from_numpy(eoff), ebs, ebs * 256, 256, 128, qp, torch.from_numpy(boff),
+                torch.from_numpy(seq), torch.from_numpy(blk), status=status)
+    assert int(status.item()) == 0
+    np.testing.assert_array_equal(qp.cpu().numpy(), qref)
+
+
+def test_flush_rejects_out_of_range_offsets(kv800):
+    """A sub-block offset past the pool is skipped by the kernel's own range check and reported in the status word:
+    the bad entry is never read or written (a host-made failure, no device fault)."""
+    B, ebs = 1, 64
+    ep = torch.zeros(10, 4, ebs, 256, dtype=torch.bfloat16, device=DEV)
+    eoff = torch.arange(10, dtype=torch.int64).view(1, 10) * 4 * ebs * 256
+    qp = torch.zeros(2, 51200, dtype=torch.uint8, device=DEV)
+    boff = torch.tensor([[51200 * 2, 0]], dtype=torch.int64)          # sub-block 0 points one past the pool
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    kv800.flush(ep, eoff, ebs, ebs * 256, 256, 128, qp, boff, torch.tensor([0]), torch.tensor([0]), status=status)
+    assert int(status.item()) & 1
+    assert int(qp.sum().item()) == 0
