@@ -208,7 +208,7 @@ def cpu_sample(layers, qs, c32, s32, S, reps=1):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="cuda", choices=("cuda", "reference"))
     ap.add_argument("--cpu-seqs", type=int, default=8, help="sequences of the CPU-baseline sample")
