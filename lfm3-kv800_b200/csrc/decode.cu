@@ -1,5 +1,6 @@
-// 800h paged GQA decode on sm_100a -- SIMT kernels: split partials over quantized sub-blocks (qdecode), over sinks +
-// exact bf16 tokens (xdecode), and the log-sum-exp merge with the in-register Hadamard (combine).
+// 800h paged GQA decode on sm_100a: split partials over quantized sub-blocks (qdecode_mma, tensor cores,
+// qdecode_mma.cuh), over sinks + exact bf16 tokens (xdecode, SIMT), and the log-sum-exp merge with the in-register
+// Hadamard (combine).
 //
 // Semantics follow the reference's torch decode (lfm3_kv800/torch_decode.py:16-80), including its two bf16 roundings
 // of every key: the dequantized pre-RoPE key is rounded to bf16 (kv800.py:86) and the rotated key is rounded to bf16
@@ -9,30 +10,11 @@
 // (kv800.py:362-383): per (row b, slot) m (log2 domain), l and acc (16 x 128, fp32); quantized slots keep V in the
 // Hadamard domain and combine() rotates their weighted sum once (kv800.py:231-236).
 #include "kv800_common.cuh"
+#include "qdecode_mma.cuh"
 
 namespace kv800 {
 
 constexpr float NEG_BIG = -1e30f;   // the reference's initial running max (kv800.py:127)
-
-struct QArgs {
-    const uint16_t* q;
-    const uint8_t* qpool;
-    int64_t qpool_bytes;
-    const int64_t* boff;
-    int64_t boff_stride;
-    const int32_t* NQ;
-    int64_t nqmax;
-    const uint16_t* cos_t;
-    const uint16_t* sin_t;
-    int64_t npos;
-    float* mo;
-    float* lo;
-    float* ao;
-    int nslots;   // slots per row in mo / lo / ao
-    int spb;      // sub-blocks per split
-    float scale;  // 128^-0.5 * log2(e)
-    int* status;
-};
 
 __device__ __forceinline__ float warp_max(float x) {
 #pragma unroll
@@ -54,142 +36,6 @@ __device__ __forceinline__ float code_x(uint32_t byte, int plane) {
 __device__ __forceinline__ void rope_pair(float k0, float k2, float cs, float sn, float& r0, float& r2) {
     r0 = bfround(fmaf(k0, cs, -(k2 * sn)));
     r2 = bfround(fmaf(k2, cs, k0 * sn));
-}
-
-// grid (B, ns), block 128: warp h = kv head h, lane = token of a 32-token tile (QK) / dims lane + 32 k (PV).
-__global__ void __launch_bounds__(128) qdecode_simt(QArgs a) {
-    const int b = blockIdx.x, s = blockIdx.y, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __shared__ float4 qs[HEADS][32][4];        // [h][j][r] = q[r][j + 32 p] for p = x, y, z, w
-    __shared__ float kA[HEADS][DIM], kB[HEADS][DIM];
-    __shared__ float4 pvs[HEADS][32];          // p * vs of token tt for the 4 rows
-    __shared__ uint4 vbs[HEADS][32];           // 16 bytes of V bits of token tt
-    for (int i = lane; i < 4 * 32; i += 32) {
-        const int r = i >> 5, j = i & 31;
-        const uint16_t* qr = a.q + ((int64_t)b * QROWS + h * 4 + r) * DIM;
-        qs[h][j][r] = make_float4(bf2f(qr[j]), bf2f(qr[j + 32]), bf2f(qr[j + 64]), bf2f(qr[j + 96]));
-    }
-    float m[4], l_lane[4], lv_lane[4], acc[4][4];
-#pragma unroll
-    for (int r = 0; r < 4; r++) {
-        m[r] = NEG_BIG;
-        l_lane[r] = lv_lane[r] = 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; k++) acc[r][k] = 0.f;
-    }
-    int64_t nq = a.NQ[b];
-    if (nq > a.nqmax) nq = a.nqmax;
-    const int64_t j0 = (int64_t)s * a.spb;
-    const int64_t j1 = min(j0 + a.spb, nq);
-    __syncwarp();
-    for (int64_t jb = j0; jb < j1; jb++) {
-        if (jb >= a.boff_stride) {
-            if (lane == 0) flag(a.status, ST_TABLE);
-            break;
-        }
-        const int64_t off = a.boff[(int64_t)b * a.boff_stride + jb];
-        const uint8_t* sb = a.qpool + off;
-        if (off < 0 || off + SUB > a.qpool_bytes || (reinterpret_cast<uintptr_t>(sb) & 15u)) {
-            if (lane == 0) flag(a.status, ST_QPOOL);
-            continue;
-        }
-#pragma unroll
-        for (int p = 0; p < 4; p++) {
-            const int c = lane + 32 * p;
-            const float sc = f8dec(sb[KSC_O + h * DIM + c]), l8 = f8dec(sb[KLO_O + h * DIM + c]);
-            kA[h][c] = 4.0f * sc;
-            kB[h][c] = l8 - 4.0f * sc;
-        }
-        __syncwarp();
-        for (int t0 = 0; t0 < BLK; t0 += 32) {
-            const int t = t0 + lane;
-            const int64_t pos = jb * BLK + t;
-            const uint4* kp = reinterpret_cast<const uint4*>(sb + KC_O + (t * HEADS + h) * 32);
-            uint4 kw0 = kp[0], kw1 = kp[1];
-            uint32_t kw[8] = {kw0.x, kw0.y, kw0.z, kw0.w, kw1.x, kw1.y, kw1.z, kw1.w};
-            uint32_t cw[16], sw[16];
-            if (pos < a.npos) {
-                const uint4* cp = reinterpret_cast<const uint4*>(a.cos_t + pos * 32);
-                const uint4* sp = reinterpret_cast<const uint4*>(a.sin_t + pos * 32);
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    uint4 c4 = cp[i], s4 = sp[i];
-                    cw[4 * i] = c4.x; cw[4 * i + 1] = c4.y; cw[4 * i + 2] = c4.z; cw[4 * i + 3] = c4.w;
-                    sw[4 * i] = s4.x; sw[4 * i + 1] = s4.y; sw[4 * i + 2] = s4.z; sw[4 * i + 3] = s4.w;
-                }
-            } else {
-                flag(a.status, ST_TABLE);
-#pragma unroll
-                for (int i = 0; i < 16; i++) cw[i] = sw[i] = 0u;
-            }
-            float sc4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int j = 0; j < 32; j++) {
-                const uint32_t byte = (kw[j >> 2] >> (8 * (j & 3))) & 0xffu;
-                const float k0 = bfround(fmaf(code_x(byte, 0), kA[h][j], kB[h][j]));
-                const float k1 = bfround(fmaf(code_x(byte, 1), kA[h][j + 32], kB[h][j + 32]));
-                const float k2 = bfround(fmaf(code_x(byte, 2), kA[h][j + 64], kB[h][j + 64]));
-                const float k3 = bfround(fmaf(code_x(byte, 3), kA[h][j + 96], kB[h][j + 96]));
-                const uint32_t cword = cw[j >> 1], sword = sw[j >> 1];
-                const float cs = __uint_as_float((j & 1) ? (cword & 0xffff0000u) : (cword << 16));
-                const float sn = __uint_as_float((j & 1) ? (sword & 0xffff0000u) : (sword << 16));
-                float r0, r2;
-                rope_pair(k0, k2, cs, sn, r0, r2);
-#pragma unroll
-                for (int r = 0; r < 4; r++) {
-                    const float4 qv = qs[h][j][r];
-                    sc4[r] = fmaf(qv.x, r0, sc4[r]);
-                    sc4[r] = fmaf(qv.y, k1, sc4[r]);
-                    sc4[r] = fmaf(qv.z, r2, sc4[r]);
-                    sc4[r] = fmaf(qv.w, k3, sc4[r]);
-                }
-            }
-            const float vl = f8dec(sb[VLO_O + t * 2 + (h >> 1)]), vs = f8dec(sb[VSC_O + t * 2 + (h >> 1)]);
-            float alpha[4], p[4];
-#pragma unroll
-            for (int r = 0; r < 4; r++) {
-                const float s2 = sc4[r] * a.scale;
-                const float mn = fmaxf(m[r], warp_max(s2));
-                alpha[r] = exp2f(m[r] - mn);
-                p[r] = exp2f(s2 - mn);
-                m[r] = mn;
-                l_lane[r] = fmaf(l_lane[r], alpha[r], p[r]);
-                lv_lane[r] = fmaf(lv_lane[r], alpha[r], p[r] * vl);
-            }
-            pvs[h][lane] = make_float4(p[0] * vs, p[1] * vs, p[2] * vs, p[3] * vs);
-            vbs[h][lane] = *reinterpret_cast<const uint4*>(sb + VB_O + (t * HEADS + h) * 16);
-            __syncwarp();
-#pragma unroll
-            for (int r = 0; r < 4; r++)
-#pragma unroll
-                for (int k = 0; k < 4; k++) acc[r][k] *= alpha[r];
-            const int jb8 = lane & 15, sh = lane >> 4;
-            for (int tt = 0; tt < 32; tt++) {
-                const float4 pv = pvs[h][tt];
-                const uint32_t byte = reinterpret_cast<const uint8_t*>(&vbs[h][tt])[jb8];
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const float bit = (float)((byte >> (sh + 2 * k)) & 1u);
-                    acc[0][k] = fmaf(bit, pv.x, acc[0][k]);
-                    acc[1][k] = fmaf(bit, pv.y, acc[1][k]);
-                    acc[2][k] = fmaf(bit, pv.z, acc[2][k]);
-                    acc[3][k] = fmaf(bit, pv.w, acc[3][k]);
-                }
-            }
-            __syncwarp();
-        }
-    }
-    const int64_t slot = (int64_t)b * a.nslots + s;
-#pragma unroll
-    for (int r = 0; r < 4; r++) {
-        const float l = warp_sum(l_lane[r]), lv = warp_sum(lv_lane[r]);
-        const int64_t row = slot * QROWS + h * 4 + r;
-        if (lane == 0) {
-            a.mo[row] = m[r];
-            a.lo[row] = l;
-        }
-#pragma unroll
-        for (int k = 0; k < 4; k++) a.ao[row * DIM + lane + 32 * k] = acc[r][k] + lv;
-    }
 }
 
 struct XArgs {
@@ -460,9 +306,9 @@ static int launch_decode_parts(const kv800_paged* P, const uint16_t* q, const ui
                                float* ao, int* status, cudaStream_t st, const char* who) {
     const int nslots = (int)(ns + nx);
     if (ns > 0) {
-        QArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
-                 mo, lo, ao, nslots, (int)spb, SCALE, status};
-        qdecode_simt<<<dim3((unsigned)B, (unsigned)ns), 128, 0, st>>>(qa);
+        QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
+                  mo, lo, ao, nslots, (int)spb, SCALE, status};
+        qdecode_mma<<<dim3((unsigned)B, (unsigned)ns), 128, 0, st>>>(qa);
         int rc = cuda_status(cudaGetLastError(), who);
         if (rc) return rc;
     }
@@ -545,9 +391,9 @@ extern "C" int kv800_qdecode(const uint16_t* q, const uint8_t* qpool, int64_t qp
         set_error("kv800_qdecode: B %lld / ns %lld above the limits", (long long)B, (long long)ns);
         return KV800_ERR_RANGE;
     }
-    QArgs qa{q, qpool, qpool_bytes, boff, boff_stride, NQ, nqmax, cos_t, sin_t, npos,
-             mo, lo, ao, (int)(ns + 1), (int)spb, scale, status};
-    qdecode_simt<<<dim3((unsigned)B, (unsigned)ns), 128, 0, as_stream(stream)>>>(qa);
+    QMArgs qa{q, qpool, qpool_bytes, boff, boff_stride, NQ, nqmax, cos_t, sin_t, npos,
+              mo, lo, ao, (int)(ns + 1), (int)spb, scale, status};
+    qdecode_mma<<<dim3((unsigned)B, (unsigned)ns), 128, 0, as_stream(stream)>>>(qa);
     return cuda_status(cudaGetLastError(), "kv800_qdecode launch");
 }
 
