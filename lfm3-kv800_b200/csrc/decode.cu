@@ -301,14 +301,27 @@ extern "C" int64_t kv800_decode_workspace_size(int64_t B, int64_t nqmax, int64_t
     return 256 + B * slots * QROWS * (int64_t)sizeof(float) * (2 + DIM) + 256;
 }
 
+static int qdecode_setup() {
+    static int done = 0;   // per process; the attribute is per function and device-independent in practice
+    if (!done) {
+        int rc = cuda_status(cudaFuncSetAttribute(qdecode_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, QM_SMEM),
+                             "qdecode_mma smem attribute");
+        if (rc) return rc;
+        done = 1;
+    }
+    return KV800_OK;
+}
+
 static int launch_decode_parts(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t, const uint16_t* sin_t,
                                int64_t npos, int64_t B, int64_t ns, int64_t spb, int64_t nx, float* mo, float* lo,
                                float* ao, int* status, cudaStream_t st, const char* who) {
     const int nslots = (int)(ns + nx);
     if (ns > 0) {
+        int rc0 = qdecode_setup();
+        if (rc0) return rc0;
         QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
                   mo, lo, ao, nslots, (int)spb, SCALE, status};
-        qdecode_mma<<<dim3((unsigned)B, (unsigned)ns), 128, 0, st>>>(qa);
+        qdecode_mma<<<dim3((unsigned)B, (unsigned)ns), 128, QM_SMEM, st>>>(qa);
         int rc = cuda_status(cudaGetLastError(), who);
         if (rc) return rc;
     }
@@ -391,9 +404,11 @@ extern "C" int kv800_qdecode(const uint16_t* q, const uint8_t* qpool, int64_t qp
         set_error("kv800_qdecode: B %lld / ns %lld above the limits", (long long)B, (long long)ns);
         return KV800_ERR_RANGE;
     }
+    int rc0 = qdecode_setup();
+    if (rc0) return rc0;
     QMArgs qa{q, qpool, qpool_bytes, boff, boff_stride, NQ, nqmax, cos_t, sin_t, npos,
               mo, lo, ao, (int)(ns + 1), (int)spb, scale, status};
-    qdecode_mma<<<dim3((unsigned)B, (unsigned)ns), 128, 0, as_stream(stream)>>>(qa);
+    qdecode_mma<<<dim3((unsigned)B, (unsigned)ns), 128, QM_SMEM, as_stream(stream)>>>(qa);
     return cuda_status(cudaGetLastError(), "kv800_qdecode launch");
 }
 

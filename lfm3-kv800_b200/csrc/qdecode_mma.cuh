@@ -12,8 +12,9 @@
 //   The exact V of a quantized token is bits * vs + vl in the Hadamard domain (kv800.py:87-91); vl enters through
 //   lv = sum_t p vl, and combine() applies H once (kv800.py:231-236).
 // Online softmax in the log2 domain per 32-token chunk; partial (m, l, acc + lv) written to the reference's slot
-// layout.  Sub-blocks are prefetched into L2 by the TMA engine (cp.async.bulk.prefetch.L2) two ahead; fragments are
-// then read with sector-exact global loads (each 32 B kc segment and 16 B vb segment once per head).
+// layout.  Sub-blocks stream into a two-stage shared-memory ring with cp.async (16-byte chunks, rows XOR-swizzled so
+// the fragment loads are bank-conflict free); per sub-block the CTA first decodes the fp8 scales once (hardware
+// e4m3x2 -> f16x2 conversion) into bf16x2 dequant constants and (vl, vs) pairs in shared memory.
 #pragma once
 #include "kv800_common.cuh"
 
@@ -119,6 +120,41 @@ struct DequantConsts {
     uint32_t L[4][4];    // [plane][pair]: bf16x2 of lo_j, lo_{j+2}
 };
 
+
+// RoPE of two key pairs with the reference's roundings, on packed bf16 operands (mixed-precision fma.rn.f32.bf16:
+// bf16 x bf16 products are exact in fp32, so t = fma(k2, sn, 0) is k2 sn and fma(k0, cs, -t) is the reference's
+// fl32(fl32(k0 cs) - fl32(k2 sn)); cvt.rn.bf16x2 is its second rounding).  k0 / k2 hold (byte j, byte j + 2) in
+// (low, high); the cos / sin of j are in the half `odd` of word ca / sa, of j + 2 in word cb / sb.
+// Ra = (kr0_j, kr2_j), Rb = (kr0_{j+2}, kr2_{j+2}).
+__device__ __forceinline__ void rope_pairs(uint32_t k0, uint32_t k2, uint32_t ca, uint32_t cb, uint32_t sa, uint32_t sb,
+                                           bool odd, uint32_t& Ra, uint32_t& Rb) {
+    if (odd) {
+        asm("{\n\t.reg .b16 k0a, k0b, k2a, k2b, x, csa, csb, sna, snb;\n\t.reg .f32 t, r0, r2;\n\t"
+            "mov.b32 {k0a, k0b}, %2;\n\tmov.b32 {k2a, k2b}, %3;\n\t"
+            "mov.b32 {x, csa}, %4;\n\tmov.b32 {x, csb}, %5;\n\tmov.b32 {x, sna}, %6;\n\tmov.b32 {x, snb}, %7;\n\t"
+            "fma.rn.f32.bf16 t, k2a, sna, 0f00000000;\n\tneg.f32 t, t;\n\tfma.rn.f32.bf16 r0, k0a, csa, t;\n\t"
+            "fma.rn.f32.bf16 t, k0a, sna, 0f00000000;\n\tfma.rn.f32.bf16 r2, k2a, csa, t;\n\t"
+            "cvt.rn.bf16x2.f32 %0, r2, r0;\n\t"
+            "fma.rn.f32.bf16 t, k2b, snb, 0f00000000;\n\tneg.f32 t, t;\n\tfma.rn.f32.bf16 r0, k0b, csb, t;\n\t"
+            "fma.rn.f32.bf16 t, k0b, snb, 0f00000000;\n\tfma.rn.f32.bf16 r2, k2b, csb, t;\n\t"
+            "cvt.rn.bf16x2.f32 %1, r2, r0;\n\t}"
+            : "=r"(Ra), "=r"(Rb)
+            : "r"(k0), "r"(k2), "r"(ca), "r"(cb), "r"(sa), "r"(sb));
+    } else {
+        asm("{\n\t.reg .b16 k0a, k0b, k2a, k2b, x, csa, csb, sna, snb;\n\t.reg .f32 t, r0, r2;\n\t"
+            "mov.b32 {k0a, k0b}, %2;\n\tmov.b32 {k2a, k2b}, %3;\n\t"
+            "mov.b32 {csa, x}, %4;\n\tmov.b32 {csb, x}, %5;\n\tmov.b32 {sna, x}, %6;\n\tmov.b32 {snb, x}, %7;\n\t"
+            "fma.rn.f32.bf16 t, k2a, sna, 0f00000000;\n\tneg.f32 t, t;\n\tfma.rn.f32.bf16 r0, k0a, csa, t;\n\t"
+            "fma.rn.f32.bf16 t, k0a, sna, 0f00000000;\n\tfma.rn.f32.bf16 r2, k2a, csa, t;\n\t"
+            "cvt.rn.bf16x2.f32 %0, r2, r0;\n\t"
+            "fma.rn.f32.bf16 t, k2b, snb, 0f00000000;\n\tneg.f32 t, t;\n\tfma.rn.f32.bf16 r0, k0b, csb, t;\n\t"
+            "fma.rn.f32.bf16 t, k0b, snb, 0f00000000;\n\tfma.rn.f32.bf16 r2, k2b, csb, t;\n\t"
+            "cvt.rn.bf16x2.f32 %1, r2, r0;\n\t}"
+            : "=r"(Ra), "=r"(Rb)
+            : "r"(k0), "r"(k2), "r"(ca), "r"(cb), "r"(sa), "r"(sb));
+    }
+}
+
 __device__ __forceinline__ void token_regs(uint32_t w0, uint32_t w1, const uint4& cw, const uint4& sw,
                                            const DequantConsts& K, uint32_t (&R)[16]) {
     const uint32_t BASE = 0x40804080u;   // bf16x2 (4.0, 4.0)
@@ -139,30 +175,74 @@ __device__ __forceinline__ void token_regs(uint32_t w0, uint32_t w1, const uint4
         const uint32_t k0 = hfma2_bf16(hsub2_bf16(x0, BASE), K.A[0][pi], K.L[0][pi]);
         const uint32_t x2 = lop3_and_or(P, 0x00300030u, BASE);
         const uint32_t k2 = hfma2_bf16(hsub2_bf16(x2, BASE), K.A[2][pi], K.L[2][pi]);
-        // the pair is (j, j + 2) with j = 8 tig + {0, 1, 4, 5}[pi]: cos word index (j - 8tig) / 2 and half (j & 1)
-        const int wi = (pi >> 1) * 2;           // words {0,1} for pi < 2, {2,3} for pi >= 2
+        // the pair is (j, j + 2) with j = 8 tig + {0, 1, 4, 5}[pi]: cos / sin words {0,1} (pi < 2) or {2,3},
+        // low halves for even j, high halves for odd j
+        const int wi = (pi >> 1) * 2;
         const bool odd = (pi & 1) != 0;
-        const float cs_a = __uint_as_float(odd ? (cwv[wi] & 0xffff0000u) : (cwv[wi] << 16));
-        const float cs_b = __uint_as_float(odd ? (cwv[wi + 1] & 0xffff0000u) : (cwv[wi + 1] << 16));
-        const float sn_a = __uint_as_float(odd ? (swv[wi] & 0xffff0000u) : (swv[wi] << 16));
-        const float sn_b = __uint_as_float(odd ? (swv[wi + 1] & 0xffff0000u) : (swv[wi + 1] << 16));
-        const float k0a = __uint_as_float(k0 << 16), k0b = __uint_as_float(k0 & 0xffff0000u);
-        const float k2a = __uint_as_float(k2 << 16), k2b = __uint_as_float(k2 & 0xffff0000u);
-        const float r0a = fmaf(k0a, cs_a, -(k2a * sn_a)), r2a = fmaf(k2a, cs_a, k0a * sn_a);
-        const float r0b = fmaf(k0b, cs_b, -(k2b * sn_b)), r2b = fmaf(k2b, cs_b, k0b * sn_b);
         const int ua = (pi & 1) | ((pi & 2) << 1);   // u of byte j = 8 tig + u
-        R[ua] = pack_bf16(r0a, r2a);
-        R[ua + 2] = pack_bf16(r0b, r2b);
+        rope_pairs(k0, k2, cwv[wi], cwv[wi + 1], swv[wi], swv[wi + 1], odd, R[ua], R[ua + 2]);
     }
 }
 
-__global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
-    const int b = blockIdx.x, s = blockIdx.y;
-    const int h = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+// ---- shared-memory staging of one sub-block (cp.async, 16-byte chunks, XOR-swizzled rows)
+// kc region: token row t (128 B = 8 chunks): chunk c stored at c ^ (t & 7).  vb region: 128-B line L (2 tokens):
+// chunk c stored at c ^ (L & 7).  A warp's fragment loads (8 tokens x one 8- or 2-byte piece of the same head) then
+// hit 8 different bank groups.  Scale region linear.
+constexpr int QM_STAGE = SUB;                        // raw bytes per stage
+constexpr int QM_CST_BYTES = HEADS * 4 * 4 * 4 * 8;  // [h][plane][tig][pair] x (A, L) bf16x2
+constexpr int QM_VSL_BYTES = BLK * 2 * 8;            // [t][group] x (vl, vs) fp32
+constexpr int QM_SMEM = 2 * QM_STAGE + QM_CST_BYTES + QM_VSL_BYTES;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ int swz_chunk(int c) {            // chunk index c of a 51,200-B sub-block -> smem chunk
+    if (c < 2048) return (c & ~7) | ((c & 7) ^ ((c >> 3) & 7));
+    if (c < 3072) {
+        const int r = c - 2048;
+        return 2048 + ((r & ~7) | ((r & 7) ^ ((r >> 3) & 7)));
+    }
+    return c;
+}
+
+__device__ __forceinline__ void stage_subblock(uint8_t* dst, const uint8_t* src, int tid) {
+    const uint32_t d0 = smem_u32(dst);
+    for (int c = tid; c < SUB / 16; c += 128) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d0 + 16 * swz_chunk(c)), "l"(src + 16 * c)
+                     : "memory");
+    }
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// two e4m3 bytes (lo = first) -> two fp32, exact (hardware e4m3 -> f16 conversion)
+__device__ __forceinline__ void e4m3x2_to_f32(uint32_t two, float& lo, float& hi) {
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"((unsigned short)two));
+    asm("{.reg .f16 l, h; mov.b32 {l, h}, %2; cvt.f32.f16 %0, l; cvt.f32.f16 %1, h;}" : "=f"(lo), "=f"(hi) : "r"(h2));
+}
+
+__device__ __forceinline__ bool sub_ok(const QMArgs& a, int b, int64_t jb, const uint8_t*& src) {
+    if (jb >= a.boff_stride) return false;
+    const int64_t off = a.boff[(int64_t)b * a.boff_stride + jb];
+    src = a.qpool + off;
+    return off >= 0 && off + SUB <= a.qpool_bytes && (reinterpret_cast<uintptr_t>(src) & 15u) == 0 &&
+           (jb + 1) * BLK <= a.npos;
+}
+
+__global__ void __launch_bounds__(128, 2) qdecode_mma(QMArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* raw0 = smem;
+    uint32_t* cst = reinterpret_cast<uint32_t*>(smem + 2 * QM_STAGE);
+    float2* vsl = reinterpret_cast<float2*>(smem + 2 * QM_STAGE + QM_CST_BYTES);
+
+    const int b = blockIdx.x, s = blockIdx.y, tid = threadIdx.x;
+    const int h = tid >> 5, lane = tid & 31, g = lane >> 2, tig = lane & 3;
     int64_t nq = a.NQ[b];
     if (nq > a.nqmax) nq = a.nqmax;
     const int64_t j0 = (int64_t)s * a.spb;
     const int64_t j1 = min(j0 + a.spb, nq);
+    const int n = (int)max((int64_t)0, j1 - j0);
 
     // ---- QK B fragments (q is bf16 already): column n = g is query row r = g of this head, zero for g >= 4
     uint32_t bq[8][2];
@@ -178,16 +258,27 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
                 bq[ks][hl] = (g < 4) ? v : 0u;
             }
     }
-    // prefetch the first sub-blocks of this split into L2
-    if (threadIdx.x == 0) {
-        for (int64_t jb = j0; jb < min(j0 + 2, j1); jb++) {
-            if (jb < a.boff_stride) {
-                const int64_t off = a.boff[(int64_t)b * a.boff_stride + jb];
-                if (off >= 0 && off + SUB <= a.qpool_bytes && ((off | reinterpret_cast<uintptr_t>(a.qpool)) & 15) == 0)
-                    prefetch_l2(a.qpool + off, SUB);
-            }
-        }
+    // ---- prologue: sub-blocks 0 and 1 of this split into the two stages
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const uint8_t* src;
+        if (i < n && sub_ok(a, b, j0 + i, src)) stage_subblock(raw0 + i * QM_STAGE, src, tid);
+        cp_commit();
     }
+
+    // per-thread shared-memory offsets inside a 16-token tile starting at a multiple of 16 (the swizzle phase
+    // (t & 7) / (L & 7) is then fixed per thread)
+    const int cc_k = 2 * h + (tig >> 1);
+    const int koff_a = g * 128 + ((cc_k ^ g) << 4) + (tig & 1) * 8;     // token t0 + g
+    const int koff_b = koff_a + 8 * 128;                                 // token t0 + g + 8
+    int voff[4];
+#pragma unroll
+    for (int q4 = 0; q4 < 4; q4++) {
+        const int L = tig + 4 * (q4 >> 1);                               // line of token t0 + 2tig + (q4&1) + 8(q4>>1)
+        const int cc = (q4 & 1) * 4 + h;
+        voff[q4] = VB_O + L * 128 + ((cc ^ L) << 4) + 2 * g;
+    }
+    const int vsl_a = 2 * g + (h >> 1), vsl_b = 2 * (g + 8) + (h >> 1);
 
     float m[2] = {-1e30f, -1e30f}, l_part[2] = {0.f, 0.f}, lv_part[2] = {0.f, 0.f};
     float acc[9][4];
@@ -196,149 +287,165 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
 #pragma unroll
         for (int e = 0; e < 4; e++) acc[i][e] = 0.f;
 
-    for (int64_t jb = j0; jb < j1; jb++) {
-        if (jb >= a.boff_stride) {
-            if (lane == 0) flag(a.status, ST_TABLE);
-            break;
-        }
-        const int64_t off = a.boff[(int64_t)b * a.boff_stride + jb];
-        const uint8_t* sb = a.qpool + off;
-        if (off < 0 || off + SUB > a.qpool_bytes || (reinterpret_cast<uintptr_t>(sb) & 15u)) {
-            if (lane == 0) flag(a.status, ST_QPOOL);
-            continue;
-        }
-        if (threadIdx.x == 0 && jb + 2 < j1 && jb + 2 < a.boff_stride) {
-            const int64_t off2 = a.boff[(int64_t)b * a.boff_stride + jb + 2];
-            if (off2 >= 0 && off2 + SUB <= a.qpool_bytes && ((off2 | reinterpret_cast<uintptr_t>(a.qpool)) & 15) == 0)
-                prefetch_l2(a.qpool + off2, SUB);
-        }
-        if ((jb + 1) * BLK > a.npos) {
-            if (lane == 0) flag(a.status, ST_TABLE);
-            break;
-        }
-        // ---- per-sub-block dequant constants for this thread's channels (bytes 8 tig .. 8 tig + 7, 4 planes)
-        DequantConsts K;
-        {
-            const uint8_t* ksc = sb + KSC_O + h * DIM;
-            const uint8_t* klo = sb + KLO_O + h * DIM;
-            const float pw[4] = {32.f, 8.f, 2.f, 8.f};   // 2^(5 - 2p) per plane (plane 3 is encoded like plane 1)
+    for (int i = 0; i < n; i++) {
+        const int64_t jb = j0 + i;
+        const uint8_t* src;
+        const bool ok = sub_ok(a, b, jb, src);
+        uint8_t* raw = raw0 + (i & 1) * QM_STAGE;
+        cp_wait<1>();
+        __syncthreads();
+        if (!ok) {
+            if (tid == 0) flag(a.status, (jb >= a.boff_stride || (jb + 1) * BLK > a.npos) ? ST_TABLE : ST_QPOOL);
+        } else {
+            // ---- cooperative preprocessing: dequant constants and (vl, vs) of this sub-block
+            const float pws[4] = {32.f, 8.f, 2.f, 8.f};   // 2^(5 - 2p); plane 3 is encoded like plane 1
 #pragma unroll
-            for (int p = 0; p < 4; p++) {
-                const uint2 scw = *reinterpret_cast<const uint2*>(ksc + 32 * p + 8 * tig);
-                const uint2 low = *reinterpret_cast<const uint2*>(klo + 32 * p + 8 * tig);
-                const uint32_t sbt[2] = {scw.x, scw.y}, lbt[2] = {low.x, low.y};
+            for (int e = 0; e < 2; e++) {
+                const int idx = tid + 128 * e;             // (hh, p, tg, pi)
+                const int pi = idx & 3, tg = (idx >> 2) & 3, p = (idx >> 4) & 3, hh = idx >> 6;
+                const int j = 8 * tg + ((pi & 1) | ((pi & 2) << 1));
+                const uint8_t* sc = raw + KSC_O + hh * DIM + 32 * p + j;
+                const uint8_t* lo = raw + KLO_O + hh * DIM + 32 * p + j;
+                float s0, s1, l0, l1;
+                e4m3x2_to_f32((uint32_t)sc[0] | ((uint32_t)sc[2] << 8), s0, s1);
+                e4m3x2_to_f32((uint32_t)lo[0] | ((uint32_t)lo[2] << 8), l0, l1);
+                const float pw = (p == 0) ? pws[0] : (p == 2) ? pws[2] : pws[1];
+                cst[2 * idx] = pack_bf16(s0 * pw, s1 * pw);
+                cst[2 * idx + 1] = pack_bf16(l0, l1);
+            }
 #pragma unroll
-                for (int pi = 0; pi < 4; pi++) {
-                    const int u = (pi & 1) | ((pi & 2) << 1);   // byte u and u + 2 of the 8
-                    const uint32_t s0 = (sbt[u >> 2] >> (8 * (u & 3))) & 0xffu;
-                    const uint32_t s1 = (sbt[(u + 2) >> 2] >> (8 * ((u + 2) & 3))) & 0xffu;
-                    const uint32_t l0 = (lbt[u >> 2] >> (8 * (u & 3))) & 0xffu;
-                    const uint32_t l1 = (lbt[(u + 2) >> 2] >> (8 * ((u + 2) & 3))) & 0xffu;
-                    K.A[p][pi] = f8_to_bf16_scaled(s0, pw[p]) | (f8_to_bf16_scaled(s1, pw[p]) << 16);
-                    K.L[p][pi] = f8_to_bf16_scaled(l0, 1.f) | (f8_to_bf16_scaled(l1, 1.f) << 16);
-                }
+            for (int e = 0; e < 2; e++) {
+                const int t = tid + 128 * e;
+                float vl0, vl1, vs0, vs1;
+                e4m3x2_to_f32(*reinterpret_cast<const uint16_t*>(raw + VLO_O + 2 * t), vl0, vl1);
+                e4m3x2_to_f32(*reinterpret_cast<const uint16_t*>(raw + VSC_O + 2 * t), vs0, vs1);
+                vsl[2 * t] = make_float2(vl0, vs0);
+                vsl[2 * t + 1] = make_float2(vl1, vs1);
             }
         }
-        const int64_t pos0 = jb * BLK;
-        // ---- 256 tokens in chunks of 32 (2 M-tiles)
+        __syncthreads();
+        if (ok) {
+            DequantConsts K;
+            {
+                const uint4* cp = reinterpret_cast<const uint4*>(cst);
+#pragma unroll
+                for (int p = 0; p < 4; p++) {
+                    const uint4 w0 = cp[((h * 4 + p) * 4 + tig) * 2];
+                    const uint4 w1 = cp[((h * 4 + p) * 4 + tig) * 2 + 1];
+                    K.A[p][0] = w0.x; K.L[p][0] = w0.y; K.A[p][1] = w0.z; K.L[p][1] = w0.w;
+                    K.A[p][2] = w1.x; K.L[p][2] = w1.y; K.A[p][3] = w1.z; K.L[p][3] = w1.w;
+                }
+            }
+            const int64_t pos0 = jb * BLK;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BLK; c0 += 32) {
-            float sc[2][4];
-            uint32_t P_lo[2], P_hi[2];
-            float vsv[2][2];
-#pragma unroll
-            for (int mt = 0; mt < 2; mt++) {
-                const int t0 = c0 + 16 * mt;
-                uint32_t R0[16], R1[16];
-                {
-                    const int ta = t0 + g, tb = t0 + g + 8;
-                    const uint2 kwa = *reinterpret_cast<const uint2*>(sb + KC_O + (ta * HEADS + h) * 32 + 8 * tig);
-                    const uint2 kwb = *reinterpret_cast<const uint2*>(sb + KC_O + (tb * HEADS + h) * 32 + 8 * tig);
-                    const uint4 ca = *reinterpret_cast<const uint4*>(a.cos_t + (pos0 + ta) * 32 + 8 * tig);
-                    const uint4 sa = *reinterpret_cast<const uint4*>(a.sin_t + (pos0 + ta) * 32 + 8 * tig);
-                    const uint4 cb = *reinterpret_cast<const uint4*>(a.cos_t + (pos0 + tb) * 32 + 8 * tig);
-                    const uint4 sbw = *reinterpret_cast<const uint4*>(a.sin_t + (pos0 + tb) * 32 + 8 * tig);
-                    token_regs(kwa.x, kwa.y, ca, sa, K, R0);
-                    token_regs(kwb.x, kwb.y, cb, sbw, K, R1);
-                }
-#pragma unroll
-                for (int e = 0; e < 4; e++) sc[mt][e] = 0.f;
-#pragma unroll
-                for (int ks = 0; ks < 8; ks++)
-                    mma_bf16(sc[mt], R0[2 * ks], R1[2 * ks], R0[2 * ks + 1], R1[2 * ks + 1], bq[ks][0], bq[ks][1]);
-                // vl / vs of tokens t0 + g and t0 + g + 8
-                vsv[mt][0] = f8dec(sb[VSC_O + (t0 + g) * 2 + (h >> 1)]);
-                vsv[mt][1] = f8dec(sb[VSC_O + (t0 + g + 8) * 2 + (h >> 1)]);
-                const float vla = f8dec(sb[VLO_O + (t0 + g) * 2 + (h >> 1)]);
-                const float vlb = f8dec(sb[VLO_O + (t0 + g + 8) * 2 + (h >> 1)]);
-                // stash vl in the P slots for now (used after the max is known)
-                P_lo[mt] = __float_as_uint(vla);
-                P_hi[mt] = __float_as_uint(vlb);
-            }
-            // ---- online softmax over the 32 tokens for this thread's rows r = 2 tig, 2 tig + 1
-            float alpha[2];
-#pragma unroll
-            for (int rr = 0; rr < 2; rr++) {
-                float mx = fmaxf(fmaxf(sc[0][rr], sc[0][rr + 2]), fmaxf(sc[1][rr], sc[1][rr + 2])) * a.scale;
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                const float mn = fmaxf(m[rr], mx);
-                alpha[rr] = exp2f(m[rr] - mn);
-                m[rr] = mn;
-            }
-            float p[2][4];
-#pragma unroll
-            for (int mt = 0; mt < 2; mt++)
-#pragma unroll
-                for (int e = 0; e < 4; e++) p[mt][e] = exp2f(fmaf(sc[mt][e], a.scale, -m[e & 1]));
-#pragma unroll
-            for (int rr = 0; rr < 2; rr++) {
-                float ls = 0.f, lvs = 0.f;
+            for (int c0 = 0; c0 < BLK; c0 += 32) {
+                float sc[2][4];
+                float vsv[2][2], vlv[2][2];
 #pragma unroll
                 for (int mt = 0; mt < 2; mt++) {
-                    ls += p[mt][rr] + p[mt][rr + 2];
-                    lvs = fmaf(p[mt][rr], __uint_as_float(P_lo[mt]), lvs);
-                    lvs = fmaf(p[mt][rr + 2], __uint_as_float(P_hi[mt]), lvs);
+                    const int t0 = c0 + 16 * mt;
+                    uint32_t R0[16], R1[16];
+                    {
+                        const uint8_t* kt = raw + t0 * 128;
+                        const uint2 kwa = *reinterpret_cast<const uint2*>(kt + koff_a);
+                        const uint2 kwb = *reinterpret_cast<const uint2*>(kt + koff_b);
+                        const uint16_t* crow = a.cos_t + (pos0 + t0 + g) * 32 + 8 * tig;
+                        const uint16_t* srow = a.sin_t + (pos0 + t0 + g) * 32 + 8 * tig;
+                        const uint4 ca = *reinterpret_cast<const uint4*>(crow);
+                        const uint4 sa = *reinterpret_cast<const uint4*>(srow);
+                        const uint4 cb = *reinterpret_cast<const uint4*>(crow + 8 * 32);
+                        const uint4 sbw = *reinterpret_cast<const uint4*>(srow + 8 * 32);
+                        token_regs(kwa.x, kwa.y, ca, sa, K, R0);
+                        token_regs(kwb.x, kwb.y, cb, sbw, K, R1);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; e++) sc[mt][e] = 0.f;
+#pragma unroll
+                    for (int ks = 0; ks < 8; ks++)
+                        mma_bf16(sc[mt], R0[2 * ks], R1[2 * ks], R0[2 * ks + 1], R1[2 * ks + 1], bq[ks][0], bq[ks][1]);
+                    const float2 xa = vsl[2 * t0 + vsl_a], xb = vsl[2 * t0 + vsl_b];
+                    vlv[mt][0] = xa.x; vsv[mt][0] = xa.y;
+                    vlv[mt][1] = xb.x; vsv[mt][1] = xb.y;
                 }
-                l_part[rr] = fmaf(l_part[rr], alpha[rr], ls);
-                lv_part[rr] = fmaf(lv_part[rr], alpha[rr], lvs);
-            }
+                // ---- online softmax over the 32 tokens for this thread's rows r = 2 tig, 2 tig + 1
+                // lazy rescale: the reference point m moves only when a score exceeds it by more than 2^6, so p <= 64
+                // and fp16(p * vs) <= 64 * 448 stays finite; the partial (m, l, acc) is exact for any m
+                float alpha[2] = {1.f, 1.f};
+                bool moved = false;
 #pragma unroll
-            for (int i = 0; i < 9; i++) {
-                acc[i][0] *= alpha[0];
-                acc[i][1] *= alpha[1];
-                acc[i][2] *= alpha[0];
-                acc[i][3] *= alpha[1];
-            }
-            // ---- PV over the two 16-token K-steps
-#pragma unroll
-            for (int mt = 0; mt < 2; mt++) {
-                const int t0 = c0 + 16 * mt;
-                // B = fp16(p * vs) transposed: rows r, tokens as K
-                const uint32_t xa = pack_f16(p[mt][0] * vsv[mt][0], p[mt][1] * vsv[mt][0]);   // token g
-                const uint32_t xb = pack_f16(p[mt][2] * vsv[mt][1], p[mt][3] * vsv[mt][1]);   // token g + 8
-                const uint32_t b0 = transpose8x8(xa), b1 = transpose8x8(xb);
-                // A: V bytes (2g, 2g + 1) of tokens t0 + 2tig, +1, +8, +9
-                const uint16_t* vrow = reinterpret_cast<const uint16_t*>(sb + VB_O + h * 16 + 2 * g);
-                const uint32_t v0 = vrow[(t0 + 2 * tig) * 32], v1 = vrow[(t0 + 2 * tig + 1) * 32];
-                const uint32_t v2 = vrow[(t0 + 2 * tig + 8) * 32], v3 = vrow[(t0 + 2 * tig + 9) * 32];
-                // byte 2g of (t, t+1) -> word A (dim row g), byte 2g+1 -> word B (dim row g + 8); shifted by 3
-                // (bytes 2 and 3 of the zero-extended 16-bit loads are zero: selector 2 fills the gaps)
-                const uint32_t wa = __byte_perm(v0, v1, 0x2420) << 3;   // (v0.b0, v1.b0)
-                const uint32_t wb = __byte_perm(v0, v1, 0x2521) << 3;   // (v0.b1, v1.b1)
-                const uint32_t wc = __byte_perm(v2, v3, 0x2420) << 3;
-                const uint32_t wd = __byte_perm(v2, v3, 0x2521) << 3;
-#pragma unroll
-                for (int i0 = 0; i0 < 8; i0++) {
-                    const uint32_t msk = 0x00080008u << i0;
-                    mma_f16(acc[i0], lop3_and_or(wa, msk, 0x38003800u), lop3_and_or(wb, msk, 0x38003800u),
-                            lop3_and_or(wc, msk, 0x38003800u), lop3_and_or(wd, msk, 0x38003800u), b0, b1);
+                for (int rr = 0; rr < 2; rr++) {
+                    float mx = fmaxf(fmaxf(sc[0][rr], sc[0][rr + 2]), fmaxf(sc[1][rr], sc[1][rr + 2])) * a.scale;
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                    if (mx > m[rr] + 6.0f) {
+                        alpha[rr] = exp2f(m[rr] - mx);
+                        m[rr] = mx;
+                        moved = true;
+                    }
                 }
-                mma_f16(acc[8], 0x38003800u, 0x38003800u, 0x38003800u, 0x38003800u, b0, b1);
+                float p[2][4];
+#pragma unroll
+                for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+                    for (int e = 0; e < 4; e++) p[mt][e] = exp2f(fmaf(sc[mt][e], a.scale, -m[e & 1]));
+                if (__any_sync(0xffffffffu, moved)) {
+#pragma unroll
+                    for (int rr = 0; rr < 2; rr++) {
+                        l_part[rr] *= alpha[rr];
+                        lv_part[rr] *= alpha[rr];
+                    }
+#pragma unroll
+                    for (int i9 = 0; i9 < 9; i9++) {
+                        acc[i9][0] *= alpha[0];
+                        acc[i9][1] *= alpha[1];
+                        acc[i9][2] *= alpha[0];
+                        acc[i9][3] *= alpha[1];
+                    }
+                }
+#pragma unroll
+                for (int rr = 0; rr < 2; rr++) {
+#pragma unroll
+                    for (int mt = 0; mt < 2; mt++) {
+                        l_part[rr] += p[mt][rr] + p[mt][rr + 2];
+                        lv_part[rr] = fmaf(p[mt][rr], vlv[mt][0], lv_part[rr]);
+                        lv_part[rr] = fmaf(p[mt][rr + 2], vlv[mt][1], lv_part[rr]);
+                    }
+                }
+                // ---- PV over the two 16-token K-steps
+#pragma unroll
+                for (int mt = 0; mt < 2; mt++) {
+                    const int t0 = c0 + 16 * mt;
+                    const uint32_t xa = pack_f16(p[mt][0] * vsv[mt][0], p[mt][1] * vsv[mt][0]);   // token g
+                    const uint32_t xb = pack_f16(p[mt][2] * vsv[mt][1], p[mt][3] * vsv[mt][1]);   // token g + 8
+                    const uint32_t b0 = transpose8x8(xa), b1 = transpose8x8(xb);
+                    // V bytes (2g, 2g + 1) of head h for tokens t0 + 2tig, +1, +8, +9 (swizzled vb lines)
+                    uint32_t v[4];
+                    const uint8_t* vt = raw + t0 * 64;
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; q4++) v[q4] = *reinterpret_cast<const uint16_t*>(vt + voff[q4]);
+                    const uint32_t wa = __byte_perm(v[0], v[1], 0x2420) << 3;   // byte 2g of (t, t + 1)
+                    const uint32_t wb = __byte_perm(v[0], v[1], 0x2521) << 3;   // byte 2g + 1
+                    const uint32_t wc = __byte_perm(v[2], v[3], 0x2420) << 3;
+                    const uint32_t wd = __byte_perm(v[2], v[3], 0x2521) << 3;
+#pragma unroll
+                    for (int i0 = 0; i0 < 8; i0++) {
+                        const uint32_t msk = 0x00080008u << i0;
+                        mma_f16(acc[i0], lop3_and_or(wa, msk, 0x38003800u), lop3_and_or(wb, msk, 0x38003800u),
+                                lop3_and_or(wc, msk, 0x38003800u), lop3_and_or(wd, msk, 0x38003800u), b0, b1);
+                    }
+                    mma_f16(acc[8], 0x38003800u, 0x38003800u, 0x38003800u, 0x38003800u, b0, b1);
+                }
             }
         }
+        __syncthreads();   // stage (i & 1) and cst / vsl free again
+        if (i + 2 < n) {
+            const uint8_t* src2;
+            if (sub_ok(a, b, jb + 2, src2)) stage_subblock(raw, src2, tid);
+        }
+        cp_commit();
     }
+    cp_wait<0>();
     // ---- finalize: rows r = 2 tig, 2 tig + 1 (valid for tig < 2)
     float l[2], lv[2];
 #pragma unroll
