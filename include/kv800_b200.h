@@ -118,6 +118,19 @@ KV800_API int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint16
                  void* stream);
 
 /*
+ * kv800_decode_noalloc -- has no counterpart in the reference.  The same decode as kv800_decode for callers that
+ * cannot allocate device memory when they decode (an engine that budgets all GPU memory in advance, a host whose
+ * allocator is out of reach on the decode thread), so they cannot pass a workspace.  The scratch is a 16 MiB array
+ * inside the library (held on every GPU that loads it until exit); a decode that needs more (see
+ * kv800_decode_workspace_size) is rejected with KV800_ERR_RANGE.  The first call on a device looks the array up
+ * with that device current, so make it before any stream capture.  All calls share the array: calls that may run
+ * at the same time on the GPU race and must be serialized by the caller.  Allocates nothing.
+ */
+KV800_API int kv800_decode_noalloc(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t,
+                                   const uint16_t* sin_t, int64_t npos, int64_t B, int64_t spb, uint16_t* out,
+                                   void* stream);
+
+/*
  * The reference's three native decode ops (kv800::qdecode / xdecode / combine, csrc/kv800_sycl.sycl:554-561) with
  * the same argument meaning and partial layout: MO / LO (B, ns + 1, 16) f32, AO (B, ns + 1, 16, 128) f32; slots
  * [0, ns) are the quantized splits (V accumulated in the Hadamard domain), slot ns the sinks + exact tokens.

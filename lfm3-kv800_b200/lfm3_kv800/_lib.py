@@ -32,6 +32,7 @@ SIGNATURES = {
     "kv800_write_exact": (_int, [_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p]),
     "kv800_decode_workspace_size": (_i64, [_i64, _i64, _i64, _i64]),
     "kv800_decode": (_int, [ctypes.POINTER(Paged), _p, _p, _p, _i64, _i64, _i64, _p, _p, _i64, _p]),
+    "kv800_decode_noalloc": (_int, [ctypes.POINTER(Paged), _p, _p, _p, _i64, _i64, _i64, _p, _p]),
     "kv800_qdecode": (_int, [_p, _p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _f, _p,
                              _p]),
     "kv800_xdecode": (_int, [_p, ctypes.POINTER(Paged), _p, _p, _i64, _p, _p, _p, _i64, _i64, _f, _p, _p]),
