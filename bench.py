@@ -308,7 +308,7 @@ def main():
     hbm, peak_kind = peaks()
     roofline = {"bound": "hbm", "achieved": round(kbytes / kdur / 1e9, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(kbytes / kdur / 1e9 / hbm, 4), "traffic": None, "peak_source": peak_kind,
-                "kernel": "qdecode_simt", "bytes_per_launch": kbytes, "launch_us": round(kdur * 1e6, 1)}
+                "kernel": "qdecode_mma", "bytes_per_launch": kbytes, "launch_us": round(kdur * 1e6, 1)}
 
     # ---- end to end through the public API with host buffers
     e2e = None

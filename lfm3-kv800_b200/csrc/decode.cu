@@ -1,5 +1,5 @@
-// 800h paged GQA decode on sm_100a: split partials over quantized sub-blocks (qdecode_mma, tensor cores,
-// qdecode_mma.cuh), over sinks + exact bf16 tokens (xdecode, SIMT), and the log-sum-exp merge with the in-register
+// 800h paged GQA decode on sm_100a: split partials over quantized sub-blocks (qdecode_mma.cuh) and over sinks +
+// exact bf16 tokens (xdecode_mma.cuh), both on the tensor cores, and the log-sum-exp merge with the in-register
 // Hadamard (combine).
 //
 // Semantics follow the reference's torch decode (lfm3_kv800/torch_decode.py:16-80), including its two bf16 roundings
@@ -11,202 +11,11 @@
 // Hadamard domain and combine() rotates their weighted sum once (kv800.py:231-236).
 #include "kv800_common.cuh"
 #include "qdecode_mma.cuh"
+#include "xdecode_mma.cuh"
 
 namespace kv800 {
 
 constexpr float NEG_BIG = -1e30f;   // the reference's initial running max (kv800.py:127)
-
-__device__ __forceinline__ float warp_max(float x) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
-    return x;
-}
-__device__ __forceinline__ float warp_sum(float x) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-    return x;
-}
-
-// 1 + c / 4 as fp32 for a 2-bit code c (mantissa bits 21-22): k = fma(x, 4 sc, lo - 4 sc) is c * sc + lo exactly.
-__device__ __forceinline__ float code_x(uint32_t byte, int plane) {
-    return __uint_as_float(0x3f800000u | (((byte >> (2 * plane)) & 3u) << 21));
-}
-
-// Rotated bf16 key pair of the reference: kr0 = bf16(k0 cs - k2 sn), kr2 = bf16(k2 cs + k0 sn).
-__device__ __forceinline__ void rope_pair(float k0, float k2, float cs, float sn, float& r0, float& r2) {
-    r0 = bfround(fmaf(k0, cs, -(k2 * sn)));
-    r2 = bfround(fmaf(k2, cs, k0 * sn));
-}
-
-struct XArgs {
-    const uint16_t* q;
-    kv800_paged P;
-    const uint16_t* cos_t;
-    const uint16_t* sin_t;
-    int64_t npos;
-    float* mo;
-    float* lo;
-    float* ao;
-    int nslots;   // slots per row
-    int slot0;    // first exact slot (= ns)
-    int nx;       // exact splits per row
-    float scale;
-    int* status;
-};
-
-// grid (B, nx), block 128: warp = kv head; split e of row b covers exact tokens [e ch, (e + 1) ch) of the row's
-// sinks + exact positions (sinks first, split 0 only).
-__global__ void __launch_bounds__(128) xdecode_simt(XArgs a) {
-    const int b = blockIdx.x, e = blockIdx.y, h = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const kv800_paged& P = a.P;
-    __shared__ float4 qx[HEADS][DIM];           // [h][d] = q rows 0..3 at dim d
-    __shared__ float4 ps[HEADS][32];            // p of token tt for the 4 rows
-    __shared__ const uint16_t* vrow[HEADS][32]; // V row of token tt (nullptr = invalid)
-    for (int d = lane; d < DIM; d += 32) {
-        const uint16_t* qr = a.q + ((int64_t)b * QROWS + h * 4) * DIM + d;
-        qx[h][d] = make_float4(bf2f(qr[0]), bf2f(qr[DIM]), bf2f(qr[2 * DIM]), bf2f(qr[3 * DIM]));
-    }
-    const int64_t n = P.N[b], nqb = P.NQ[b];
-    int64_t lo_e = nqb * BLK;
-    if (P.win && n - P.win > lo_e) lo_e = n - P.win;
-    int64_t cnt = 0;
-    if (P.win && P.sk) {
-        cnt = P.nsink;
-        if (lo_e < cnt) cnt = lo_e;
-        if (n < cnt) cnt = n;
-        if (cnt < 0) cnt = 0;
-    }
-    const int64_t E = n > lo_e ? n - lo_e : 0;            // exact positions [lo_e, n)
-    const int64_t ch = (E + a.nx - 1) / a.nx;
-    const int64_t x0 = min((int64_t)e * ch, E), x1 = min(x0 + ch, E);
-    const int64_t s0 = (e == 0) ? 0 : cnt;                 // token list of this split: [s0, cnt) sinks + exact
-    const int64_t total = (cnt - s0) + (x1 - x0);
-    float m[4], l_lane[4], acc[4][4];
-#pragma unroll
-    for (int r = 0; r < 4; r++) {
-        m[r] = NEG_BIG;
-        l_lane[r] = 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; k++) acc[r][k] = 0.f;
-    }
-    __syncwarp();
-    for (int64_t t0 = 0; t0 < total; t0 += 32) {
-        const int64_t ti = t0 + lane;
-        const uint16_t* kr = nullptr;
-        const uint16_t* vr = nullptr;
-        int64_t pos = 0;
-        if (ti < total) {
-            if (ti < cnt - s0) {
-                const int64_t t = s0 + ti;
-                pos = t;
-                const int64_t ko = P.skoff[b] + (t * HEADS + h) * DIM, vo = P.svoff[b] + (t * HEADS + h) * DIM;
-                if (ko >= 0 && ko + DIM <= P.sk_elems && vo >= 0 && vo + DIM <= P.sv_elems) {
-                    kr = P.sk + ko;
-                    vr = P.sv + vo;
-                } else {
-                    flag(a.status, ST_SINK);
-                }
-            } else {
-                pos = lo_e + x0 + (ti - (cnt - s0));
-                if (pos / P.ebs < P.eoff_stride) {
-                    const int64_t ko = P.eoff[(int64_t)b * P.eoff_stride + pos / P.ebs] + h * P.e_hs + (pos % P.ebs) * P.e_ts;
-                    if (ko >= 0 && ko + DIM <= P.epool_elems && ko + P.e_v >= 0 && ko + P.e_v + DIM <= P.epool_elems) {
-                        kr = P.epool + ko;
-                        vr = P.epool + ko + P.e_v;
-                    } else {
-                        flag(a.status, ST_EPOOL);
-                    }
-                } else {
-                    flag(a.status, ST_TABLE);
-                }
-            }
-            if (kr && pos >= a.npos) {
-                flag(a.status, ST_TABLE);
-                kr = vr = nullptr;
-            }
-        }
-        float s2[4];
-        if (kr) {
-            float kv[DIM];
-#pragma unroll
-            for (int d = 0; d < DIM; d++) kv[d] = bf2f(kr[d]);
-#pragma unroll
-            for (int j = 0; j < 32; j++) {
-                const float cs = bf2f(a.cos_t[pos * 32 + j]), sn = bf2f(a.sin_t[pos * 32 + j]);
-                float r0, r2;
-                rope_pair(kv[j], kv[j + 64], cs, sn, r0, r2);
-                kv[j] = r0;
-                kv[j + 64] = r2;
-            }
-            float sc4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int d = 0; d < DIM; d++) {
-                const float4 qv = qx[h][d];
-                sc4[0] = fmaf(qv.x, kv[d], sc4[0]);
-                sc4[1] = fmaf(qv.y, kv[d], sc4[1]);
-                sc4[2] = fmaf(qv.z, kv[d], sc4[2]);
-                sc4[3] = fmaf(qv.w, kv[d], sc4[3]);
-            }
-#pragma unroll
-            for (int r = 0; r < 4; r++) s2[r] = sc4[r] * a.scale;
-        } else {
-#pragma unroll
-            for (int r = 0; r < 4; r++) s2[r] = -__int_as_float(0x7f800000);
-        }
-        float alpha[4], p[4];
-#pragma unroll
-        for (int r = 0; r < 4; r++) {
-            const float mn = fmaxf(m[r], warp_max(s2[r]));
-            alpha[r] = exp2f(m[r] - mn);
-            p[r] = exp2f(s2[r] - mn);
-            m[r] = mn;
-            l_lane[r] = fmaf(l_lane[r], alpha[r], p[r]);
-        }
-        ps[h][lane] = make_float4(p[0], p[1], p[2], p[3]);
-        vrow[h][lane] = vr;
-        __syncwarp();
-#pragma unroll
-        for (int r = 0; r < 4; r++)
-#pragma unroll
-            for (int k = 0; k < 4; k++) acc[r][k] *= alpha[r];
-        const int nt = (int)min((int64_t)32, total - t0);
-        for (int tt = 0; tt < nt; tt++) {
-            const uint16_t* v = vrow[h][tt];
-            if (!v) continue;
-            const float4 pv = ps[h][tt];
-            float x[4];
-            if ((reinterpret_cast<uintptr_t>(v) & 7u) == 0) {
-                const uint2 w = *reinterpret_cast<const uint2*>(v + 4 * lane);
-                x[0] = __uint_as_float(w.x << 16);
-                x[1] = __uint_as_float(w.x & 0xffff0000u);
-                x[2] = __uint_as_float(w.y << 16);
-                x[3] = __uint_as_float(w.y & 0xffff0000u);
-            } else {
-#pragma unroll
-                for (int k = 0; k < 4; k++) x[k] = bf2f(v[4 * lane + k]);
-            }
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                acc[0][k] = fmaf(pv.x, x[k], acc[0][k]);
-                acc[1][k] = fmaf(pv.y, x[k], acc[1][k]);
-                acc[2][k] = fmaf(pv.z, x[k], acc[2][k]);
-                acc[3][k] = fmaf(pv.w, x[k], acc[3][k]);
-            }
-        }
-        __syncwarp();
-    }
-    const int64_t slot = (int64_t)b * a.nslots + a.slot0 + e;
-#pragma unroll
-    for (int r = 0; r < 4; r++) {
-        const float l = warp_sum(l_lane[r]);
-        const int64_t row = slot * QROWS + h * 4 + r;
-        if (lane == 0) {
-            a.mo[row] = m[r];
-            a.lo[row] = l;
-        }
-        *reinterpret_cast<float4*>(a.ao + row * DIM + 4 * lane) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
-    }
-}
 
 // grid (B), block 512: warp = query row r; lane = dims 4 lane .. 4 lane + 3.  Slots [0, ns) are quantized (Hadamard
 // domain), [ns, nslots) exact.  o = (sum_{s<ns} w_s acc_s) H + sum_{s>=ns} w_s acc_s, w_s = exp2(m_s - max m),
@@ -312,6 +121,17 @@ static int qdecode_setup() {
     return KV800_OK;
 }
 
+static int xdecode_setup() {
+    static int done = 0;
+    if (!done) {
+        int rc = cuda_status(cudaFuncSetAttribute(xdecode_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, XM_SMEM),
+                             "xdecode_mma smem attribute");
+        if (rc) return rc;
+        done = 1;
+    }
+    return KV800_OK;
+}
+
 static int launch_decode_parts(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t, const uint16_t* sin_t,
                                int64_t npos, int64_t B, int64_t ns, int64_t spb, int64_t nx, float* mo, float* lo,
                                float* ao, int* status, cudaStream_t st, const char* who) {
@@ -325,8 +145,10 @@ static int launch_decode_parts(const kv800_paged* P, const uint16_t* q, const ui
         int rc = cuda_status(cudaGetLastError(), who);
         if (rc) return rc;
     }
-    XArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, nslots, (int)ns, (int)nx, SCALE, status};
-    xdecode_simt<<<dim3((unsigned)B, (unsigned)nx), 128, 0, st>>>(xa);
+    int rcx = xdecode_setup();
+    if (rcx) return rcx;
+    XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, nslots, (int)ns, (int)nx, SCALE, status};
+    xdecode_mma<<<dim3((unsigned)B, (unsigned)nx), 128, XM_SMEM, st>>>(xa);
     return cuda_status(cudaGetLastError(), who);
 }
 
@@ -346,6 +168,10 @@ extern "C" int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint1
     }
     if ((reinterpret_cast<uintptr_t>(cos_t) | reinterpret_cast<uintptr_t>(sin_t)) & 15u) {
         set_error("kv800_decode: cos / sin tables must be 16-byte aligned");
+        return KV800_ERR_ARG;
+    }
+    if (reinterpret_cast<uintptr_t>(q) & 15u) {
+        set_error("kv800_decode: q must be 16-byte aligned");
         return KV800_ERR_ARG;
     }
     if (reinterpret_cast<uintptr_t>(out) & 7u) {
@@ -434,8 +260,10 @@ extern "C" int kv800_xdecode(const uint16_t* q, const kv800_paged* P, const uint
         set_error("kv800_xdecode: B %lld above the limit", (long long)B);
         return KV800_ERR_RANGE;
     }
-    XArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, (int)(ns + 1), (int)ns, 1, scale, status};
-    xdecode_simt<<<dim3((unsigned)B, 1), 128, 0, as_stream(stream)>>>(xa);
+    int rcx = xdecode_setup();
+    if (rcx) return rcx;
+    XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, (int)(ns + 1), (int)ns, 1, scale, status};
+    xdecode_mma<<<dim3((unsigned)B, 1), 128, XM_SMEM, as_stream(stream)>>>(xa);
     return cuda_status(cudaGetLastError(), "kv800_xdecode launch");
 }
 

@@ -1,0 +1,307 @@
+// Exact-token decode partial on the tensor cores (mma.sync m16n8k16, bf16), sm_100a: the sinks and exact bf16 tokens
+// of one (row b, split e), all 4 kv heads (warp = head), in 16-token tiles.
+//
+//   gather   per tile, 16 tokens x 4 heads x (K row, V row) of 256 B plus the tile's cos / sin rows are copied with
+//            cp.async (16-byte chunks) into a two-stage shared-memory ring; rows are XOR-swizzled by (token & 7) in
+//            16-byte chunks so ldmatrix reads are bank-conflict free.  Rows that fail the range / alignment checks are
+//            zero-filled (cp.async src-size 0) and masked out of the softmax.
+//   QK       A = the tile's K rows via ldmatrix.x4 (dims on K); the RoPE dims (d, d + 64), d < 32, are rotated in
+//            registers with the reference's roundings (torch_decode.py:16-24): fma.rn.f32.bf16 gives
+//            fl32(k0 cs - k2 sn) exactly, cvt.rn.bf16x2 the bf16 rounding.  B = q (bf16, columns 4..7 zero).
+//   PV       A = V^T via ldmatrix.x4.trans (dims on M, tokens on K), B = P transposed from the QK accumulator with
+//            movmatrix, split into bf16 hi + lo (P - hi) so the products keep ~16 bits of P; fp32 accumulate.
+// Online softmax in the log2 domain with a lazily moved reference point (as in qdecode_mma).  The partial (m, l, acc)
+// goes to slot slot0 + e of the reference's layout (kv800.py:224-228 for the single-split form).
+#pragma once
+#include "qdecode_mma.cuh"
+
+namespace kv800 {
+
+struct XMArgs {
+    const uint16_t* q;
+    kv800_paged P;
+    const uint16_t* cos_t;
+    const uint16_t* sin_t;
+    int64_t npos;
+    float* mo;
+    float* lo;
+    float* ao;
+    int nslots;
+    int slot0;
+    int nx;
+    float scale;
+    int* status;
+};
+
+constexpr int XM_TILE = 16;
+constexpr int XM_KV_BYTES = HEADS * XM_TILE * 256;          // one of K / V for a tile: 16 KB
+constexpr int XM_CS_BYTES = XM_TILE * 64;                   // cos (or sin) rows of a tile
+constexpr int XM_STAGE = 2 * XM_KV_BYTES + 2 * XM_CS_BYTES;  // 34,816 B
+constexpr int XM_SMEM = 2 * XM_STAGE;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void cp16(uint32_t dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+
+// RoPE of one register pair on the A fragment: k0 = (K[d], K[d+1]), k2 = (K[d+64], K[d+65]) of one token row,
+// c / s = (cos, sin) of frequencies (d, d+1).  Returns kr0 pair in k0, kr2 pair in k2 (bf16, reference roundings).
+__device__ __forceinline__ void rope_frag(uint32_t& k0, uint32_t& k2, uint32_t c, uint32_t s) {
+    uint32_t r0, r2;
+    asm("{\n\t.reg .b16 a0, a1, b0, b1, c0, c1, s0, s1;\n\t.reg .f32 t, x0, x1, y0, y1;\n\t"
+        "mov.b32 {a0, a1}, %2;\n\tmov.b32 {b0, b1}, %3;\n\tmov.b32 {c0, c1}, %4;\n\tmov.b32 {s0, s1}, %5;\n\t"
+        "fma.rn.f32.bf16 t, b0, s0, 0f00000000;\n\tneg.f32 t, t;\n\tfma.rn.f32.bf16 x0, a0, c0, t;\n\t"
+        "fma.rn.f32.bf16 t, b1, s1, 0f00000000;\n\tneg.f32 t, t;\n\tfma.rn.f32.bf16 x1, a1, c1, t;\n\t"
+        "fma.rn.f32.bf16 t, a0, s0, 0f00000000;\n\tfma.rn.f32.bf16 y0, b0, c0, t;\n\t"
+        "fma.rn.f32.bf16 t, a1, s1, 0f00000000;\n\tfma.rn.f32.bf16 y1, b1, c1, t;\n\t"
+        "cvt.rn.bf16x2.f32 %0, x1, x0;\n\tcvt.rn.bf16x2.f32 %1, y1, y0;\n\t}"
+        : "=r"(r0), "=r"(r2)
+        : "r"(k0), "r"(k2), "r"(c), "r"(s));
+    k0 = r0;
+    k2 = r2;
+}
+
+// smem byte offset of (row r, 16-byte chunk c) in a [16 rows][256 B] swizzled tile
+__device__ __forceinline__ int xm_off(int r, int c) { return r * 256 + ((c ^ (r & 7)) << 4); }
+
+__global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int b = blockIdx.x, e = blockIdx.y, tid = threadIdx.x;
+    const int h = tid >> 5, lane = tid & 31, g = lane >> 2, tig = lane & 3;
+    const kv800_paged& P = a.P;
+
+    // ---- this split's token list: [s0, cnt) sinks, then exact positions lo_e + [x0, x1)
+    const int64_t n = P.N[b], nqb = P.NQ[b];
+    int64_t lo_e = nqb * BLK;
+    if (P.win && n - P.win > lo_e) lo_e = n - P.win;
+    int64_t cnt = 0;
+    if (P.win && P.sk) {
+        cnt = P.nsink;
+        if (lo_e < cnt) cnt = lo_e;
+        if (n < cnt) cnt = n;
+        if (cnt < 0) cnt = 0;
+    }
+    const int64_t E = n > lo_e ? n - lo_e : 0;
+    const int64_t ch = (E + a.nx - 1) / a.nx;
+    const int64_t x0 = min((int64_t)e * ch, E), x1 = min(x0 + ch, E);
+    const int64_t s0 = (e == 0) ? 0 : cnt;
+    const int64_t nsk = cnt - s0;
+    const int64_t total = nsk + (x1 - x0);
+    const int ntiles = (int)((total + XM_TILE - 1) / XM_TILE);
+
+    // ---- issue the copies of tile `it` into stage `st`; returns nothing, validity lands in smem (zero rows)
+    // thread = (token tt = tid / 8, row role sub = tid % 8: head sub / 2, K (sub even) or V (odd)); plus one cos / sin
+    // chunk per thread (token tid / 8, table (tid / 4) & 1, chunk tid & 3)
+    auto issue = [&](int it, int st) {
+        uint8_t* base = smem + st * XM_STAGE;
+        const int tt = tid >> 3, sub = tid & 7, hh = sub >> 1, isv = sub & 1;
+        const int64_t ti = (int64_t)it * XM_TILE + tt;
+        const uint16_t* row = P.epool;
+        bool ok = false;
+        int64_t pos = 0;
+        if (ti < total) {
+            if (ti < nsk) {
+                const int64_t t = s0 + ti;
+                pos = t;
+                const int64_t o = (isv ? P.svoff[b] : P.skoff[b]) + (t * HEADS + hh) * DIM;
+                const int64_t lim = isv ? P.sv_elems : P.sk_elems;
+                const uint16_t* pool = isv ? P.sv : P.sk;
+                if (o >= 0 && o + DIM <= lim) {
+                    row = pool + o;
+                    ok = true;
+                } else if (sub == 0) {
+                    flag(a.status, ST_SINK);
+                }
+            } else {
+                pos = lo_e + x0 + (ti - nsk);
+                if (pos / P.ebs < P.eoff_stride) {
+                    const int64_t o = P.eoff[(int64_t)b * P.eoff_stride + pos / P.ebs] + hh * P.e_hs +
+                                      (pos % P.ebs) * P.e_ts + (isv ? P.e_v : 0);
+                    if (o >= 0 && o + DIM <= P.epool_elems) {
+                        row = P.epool + o;
+                        ok = true;
+                    } else if (sub == 0) {
+                        flag(a.status, ST_EPOOL);
+                    }
+                } else if (sub == 0) {
+                    flag(a.status, ST_TABLE);
+                }
+            }
+            if (ok && pos >= a.npos) {
+                if (sub == 0) flag(a.status, ST_TABLE);
+                ok = false;
+            }
+            if (ok && (reinterpret_cast<uintptr_t>(row) & 15u)) {
+                if (sub == 0) flag(a.status, ST_EPOOL);
+                ok = false;
+            }
+        }
+        const uint32_t dst = smem_u32(base + isv * XM_KV_BYTES + hh * (XM_TILE * 256));
+#pragma unroll
+        for (int c = 0; c < 16; c++) cp16(dst + xm_off(tt, c), ok ? (const void*)(row + 8 * c) : (const void*)P.epool, ok);
+        // cos / sin rows: token tid / 8 ... one chunk per thread
+        {
+            const int tc = tid >> 3, which = (tid >> 2) & 1, c4 = tid & 3;
+            const int64_t tj = (int64_t)it * XM_TILE + tc;
+            int64_t pj = -1;
+            if (tj < total) pj = (tj < nsk) ? (s0 + tj) : (lo_e + x0 + (tj - nsk));
+            const bool okc = pj >= 0 && pj < a.npos;
+            const uint16_t* tab = which ? a.sin_t : a.cos_t;
+            const uint32_t d = smem_u32(base + 2 * XM_KV_BYTES + which * XM_CS_BYTES + tc * 64 + c4 * 16);
+            cp16(d, okc ? (const void*)(tab + pj * 32 + c4 * 8) : (const void*)a.cos_t, okc);
+        }
+    };
+
+    // ---- q B fragments (standard dims layout): b0 = q[g][16 ks + 2 tig ..], b1 = q[g][16 ks + 8 + 2 tig ..]
+    uint32_t bq[8][2];
+    {
+        const uint16_t* qr = a.q + ((int64_t)b * QROWS + h * 4 + (g & 3)) * DIM;
+#pragma unroll
+        for (int ks = 0; ks < 8; ks++) {
+            const uint32_t v0 = *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 2 * tig);
+            const uint32_t v1 = *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 8 + 2 * tig);
+            bq[ks][0] = (g < 4) ? v0 : 0u;
+            bq[ks][1] = (g < 4) ? v1 : 0u;
+        }
+    }
+    if (ntiles > 0) issue(0, 0);
+    cp_commit();
+    if (ntiles > 1) issue(1, 1);
+    cp_commit();
+
+    float m[2] = {-1e30f, -1e30f}, l_part[2] = {0.f, 0.f};
+    float acc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int k = 0; k < 4; k++) acc[i][k] = 0.f;
+
+    // ldmatrix lane roles: matrix mi = lane / 8, row-in-matrix ri = lane % 8
+    const int mi = lane >> 3, ri = lane & 7;
+    for (int it = 0; it < ntiles; it++) {
+        const int st = it & 1;
+        cp_wait<1>();
+        __syncthreads();
+        const uint8_t* base = smem + st * XM_STAGE;
+        const uint32_t kb = smem_u32(base + h * (XM_TILE * 256));
+        const uint32_t vb = smem_u32(base + XM_KV_BYTES + h * (XM_TILE * 256));
+        const uint32_t* cs = reinterpret_cast<const uint32_t*>(base + 2 * XM_KV_BYTES);
+        const uint32_t* sn = reinterpret_cast<const uint32_t*>(base + 2 * XM_KV_BYTES + XM_CS_BYTES);
+        // ---- QK: A fragments of the 8 K-steps (matrices: rows 0-7 / 8-15 x dims +0 / +8)
+        uint32_t A[8][4];
+#pragma unroll
+        for (int ks = 0; ks < 8; ks++) {
+            const int r = (mi & 1) * 8 + ri, c = 2 * ks + (mi >> 1);
+            ldsm_x4(kb + xm_off(r, c), A[ks][0], A[ks][1], A[ks][2], A[ks][3]);
+        }
+        // RoPE on K-steps 0,1 (dims 0..31) with 4,5 (dims 64..95): regs 0 / 2 are token g, 1 / 3 token g + 8;
+        // regs 0 / 1 cover dims 16 ks + 2 tig, regs 2 / 3 dims 16 ks + 8 + 2 tig
+#pragma unroll
+        for (int ks = 0; ks < 2; ks++)
+#pragma unroll
+            for (int rg = 0; rg < 4; rg++) {
+                const int tok = g + 8 * (rg & 1);
+                const int d = 16 * ks + 8 * (rg >> 1) + 2 * tig;   // even, < 32
+                rope_frag(A[ks][rg], A[ks + 4][rg], cs[tok * 16 + (d >> 1)], sn[tok * 16 + (d >> 1)]);
+            }
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 8; ks++) mma_bf16(sc, A[ks][0], A[ks][1], A[ks][2], A[ks][3], bq[ks][0], bq[ks][1]);
+        // mask tokens past the list end or without valid rows (zero-filled rows still give finite scores, but the
+        // list end is the only place rows are missing when the tables are consistent)
+        const int64_t t_a = (int64_t)it * XM_TILE + g, t_b = t_a + 8;
+        float s2[4];
+        s2[0] = (t_a < total) ? sc[0] * a.scale : -__int_as_float(0x7f800000);
+        s2[1] = (t_a < total) ? sc[1] * a.scale : -__int_as_float(0x7f800000);
+        s2[2] = (t_b < total) ? sc[2] * a.scale : -__int_as_float(0x7f800000);
+        s2[3] = (t_b < total) ? sc[3] * a.scale : -__int_as_float(0x7f800000);
+        float alpha[2] = {1.f, 1.f};
+        bool moved = false;
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            float mx = fmaxf(s2[rr], s2[rr + 2]);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            if (mx > m[rr] + 6.0f) {
+                alpha[rr] = exp2f(m[rr] - mx);
+                m[rr] = mx;
+                moved = true;
+            }
+        }
+        float p[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) p[k] = exp2f(s2[k] - m[k & 1]);
+        if (__any_sync(0xffffffffu, moved)) {
+            l_part[0] *= alpha[0];
+            l_part[1] *= alpha[1];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                acc[i][0] *= alpha[0];
+                acc[i][1] *= alpha[1];
+                acc[i][2] *= alpha[0];
+                acc[i][3] *= alpha[1];
+            }
+        }
+        l_part[0] += p[0] + p[2];
+        l_part[1] += p[1] + p[3];
+        // ---- PV: B = P^T (hi + lo bf16), A = V^T via ldmatrix.trans
+        const uint32_t ha = pack_bf16(p[0], p[1]), hb = pack_bf16(p[2], p[3]);
+        const uint32_t la = pack_bf16(p[0] - __uint_as_float(ha << 16), p[1] - __uint_as_float(ha & 0xffff0000u));
+        const uint32_t lb = pack_bf16(p[2] - __uint_as_float(hb << 16), p[3] - __uint_as_float(hb & 0xffff0000u));
+        const uint32_t bh0 = transpose8x8(ha), bh1 = transpose8x8(hb);
+        const uint32_t bl0 = transpose8x8(la), bl1 = transpose8x8(lb);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            // matrices: (tokens 0-7, dims +0), (tokens 0-7, dims +8), (tokens 8-15, dims +0), (tokens 8-15, dims +8)
+            const int r = (mi >> 1) * 8 + ri, c = 2 * i + (mi & 1);
+            uint32_t v0, v1, v2, v3;
+            ldsm_x4_t(vb + xm_off(r, c), v0, v1, v2, v3);
+            mma_bf16(acc[i], v0, v1, v2, v3, bh0, bh1);
+            mma_bf16(acc[i], v0, v1, v2, v3, bl0, bl1);
+        }
+        __syncthreads();
+        if (it + 2 < ntiles) issue(it + 2, st);
+        cp_commit();
+    }
+    cp_wait<0>();
+    // ---- partial: rows r = 2 tig, 2 tig + 1 (valid for tig < 2); acc[i] rows d = 16 i + g, 16 i + g + 8
+    float l[2];
+#pragma unroll
+    for (int rr = 0; rr < 2; rr++) {
+        float x = l_part[rr];
+        x += __shfl_xor_sync(0xffffffffu, x, 4);
+        x += __shfl_xor_sync(0xffffffffu, x, 8);
+        x += __shfl_xor_sync(0xffffffffu, x, 16);
+        l[rr] = x;
+    }
+    if (tig < 2) {
+        const int64_t slot = (int64_t)b * a.nslots + a.slot0 + e;
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            const int64_t row = slot * QROWS + h * 4 + 2 * tig + rr;
+            if (g == 0) {
+                a.mo[row] = m[rr];
+                a.lo[row] = l[rr];
+            }
+            float* o = a.ao + row * DIM;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                o[16 * i + g] = acc[i][rr];
+                o[16 * i + g + 8] = acc[i][rr + 2];
+            }
+        }
+    }
+}
+
+}  // namespace kv800
