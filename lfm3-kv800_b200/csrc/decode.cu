@@ -17,27 +17,104 @@ namespace kv800 {
 
 constexpr float NEG_BIG = -1e30f;   // the reference's initial running max (kv800.py:127)
 
-// grid (B), block 512: warp = query row r; lane = dims 4 lane .. 4 lane + 3.  Slots [0, ns) are quantized (Hadamard
-// domain), [ns, nslots) exact.  o = (sum_{s<ns} w_s acc_s) H + sum_{s>=ns} w_s acc_s, w_s = exp2(m_s - max m),
-// out = bf16(o / sum_s w_s l_s) (kv800.py:231-236); a row with no keys at all gives zeros (torch_decode.py:71-72).
-__global__ void __launch_bounds__(512) combine_kernel(const float* mo, const float* lo, const float* ao, int ns,
-                                                      int nslots, uint16_t* out) {
+// Where the partials of row b live.  Quantized slots: grid mode (prefix == nullptr) b * qstride + s for s < ns;
+// persistent mode c + b for the CTAs c whose unit range meets row b's units [prefix[b], prefix[b + 1]).  Exact slots:
+// xbase + b * xstride + e for e < nx.
+struct SlotMap {
+    int ns;
+    int64_t qstride;
+    const int64_t* prefix;
+    int64_t B;
+    int64_t G0;
+    int64_t xbase, xstride;
+    int nx;
+};
+
+// prefix[b] = sum over rows < b of clamp(min(NQ, nqmax), 0); prefix[B] = W.  One CTA of 1024 threads.
+__global__ void __launch_bounds__(1024) qsched_kernel(const int32_t* NQ, int64_t nqmax, int64_t B, int64_t* prefix) {
+    __shared__ int64_t wsum[32];
+    __shared__ int64_t carry;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) carry = 0;
+    __syncthreads();
+    for (int64_t base = 0; base < B; base += 1024) {
+        int64_t v = 0;
+        if (base + tid < B) {
+            v = NQ[base + tid];
+            if (v > nqmax) v = nqmax;
+            if (v < 0) v = 0;
+        }
+        int64_t x = v;   // inclusive scan within the warp
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int64_t y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) wsum[warp] = x;
+        __syncthreads();
+        if (warp == 0) {
+            int64_t w = wsum[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int64_t y = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o) w += y;
+            }
+            wsum[lane] = w;   // inclusive over warps
+        }
+        __syncthreads();
+        const int64_t excl = carry + (warp ? wsum[warp - 1] : 0) + x - v;
+        if (base + tid < B) prefix[base + tid] = excl;
+        __syncthreads();
+        if (tid == 0) carry += wsum[31];
+        __syncthreads();
+    }
+    if (tid == 0) prefix[B] = carry;
+}
+
+// grid (B), block 512: warp = query row r; lane = dims 4 lane .. 4 lane + 3.
+// o = (sum_{quantized} w_s acc_s) H + sum_{exact} w_s acc_s, w_s = exp2(m_s - max m), out = bf16(o / sum_s w_s l_s)
+// (kv800.py:231-236); a row with no keys at all gives zeros (torch_decode.py:71-72).
+__global__ void __launch_bounds__(512) combine_kernel(const float* mo, const float* lo, const float* ao, SlotMap sm,
+                                                      uint16_t* out) {
     const int b = blockIdx.x, r = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int64_t q0 = 0, nqs = 0;   // quantized slots: grid q0 + s * 1, persistent (c0 + b) + i
+    if (sm.prefix == nullptr) {
+        q0 = (int64_t)b * sm.qstride;
+        nqs = sm.ns;
+    } else {
+        const int64_t W = sm.prefix[sm.B];
+        const int64_t rs = sm.prefix[b], re = sm.prefix[b + 1];
+        if (W > 0 && re > rs) {
+            const int64_t G = min(sm.G0, W);
+            const int64_t cf = ((rs + 1) * G - 1) / W, cl = (re * G - 1) / W;
+            q0 = cf + b;
+            nqs = cl - cf + 1;
+        }
+    }
+    const int64_t x0 = sm.xbase + (int64_t)b * sm.xstride;
     float M = NEG_BIG;
-    for (int s = 0; s < nslots; s++) M = fmaxf(M, mo[((int64_t)b * nslots + s) * QROWS + r]);
+    for (int64_t i = 0; i < nqs; i++) M = fmaxf(M, mo[(q0 + i) * QROWS + r]);
+    for (int e = 0; e < sm.nx; e++) M = fmaxf(M, mo[(x0 + e) * QROWS + r]);
     float L = 0.f, oq[4] = {0.f, 0.f, 0.f, 0.f}, oe[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int s = 0; s < nslots; s++) {
-        const int64_t row = ((int64_t)b * nslots + s) * QROWS + r;
+    for (int64_t i = 0; i < nqs + sm.nx; i++) {
+        const bool isq = i < nqs;
+        const int64_t row = (isq ? q0 + i : x0 + (i - nqs)) * QROWS + r;
         const float w = exp2f(mo[row] - M);
         L = fmaf(w, lo[row], L);
         const float4 x = *reinterpret_cast<const float4*>(ao + row * DIM + 4 * lane);
-        float* o = s < ns ? oq : oe;
-        o[0] = fmaf(w, x.x, o[0]);
-        o[1] = fmaf(w, x.y, o[1]);
-        o[2] = fmaf(w, x.z, o[2]);
-        o[3] = fmaf(w, x.w, o[3]);
+        if (isq) {
+            oq[0] = fmaf(w, x.x, oq[0]);
+            oq[1] = fmaf(w, x.y, oq[1]);
+            oq[2] = fmaf(w, x.z, oq[2]);
+            oq[3] = fmaf(w, x.w, oq[3]);
+        } else {
+            oe[0] = fmaf(w, x.x, oe[0]);
+            oe[1] = fmaf(w, x.y, oe[1]);
+            oe[2] = fmaf(w, x.z, oe[2]);
+            oe[3] = fmaf(w, x.w, oe[3]);
+        }
     }
-    if (ns > 0) {
+    if (nqs > 0) {
         // 128-point Sylvester Hadamard: dims d = 4 lane + e; stages 1, 2 in-lane, 4 .. 64 across lanes 1 .. 16
         float a0 = oq[0] + oq[1], a1 = oq[0] - oq[1], a2 = oq[2] + oq[3], a3 = oq[2] - oq[3];
         oq[0] = a0 + a2; oq[2] = a0 - a2; oq[1] = a1 + a3; oq[3] = a1 - a3;
@@ -69,15 +146,21 @@ using namespace kv800;
 
 namespace {
 constexpr int64_t MAX_B = 1 << 20;
-constexpr int NX_DEFAULT = 4;   // exact splits per row in kv800_decode
+constexpr int NX_DEFAULT = 4;                   // exact splits per row in kv800_decode
 constexpr float SCALE = 0.12751743074602467f;   // 128^-0.5 * log2(e)
+constexpr int MAX_DEV = 64;
 
-int64_t choose_spb(int64_t B, int64_t nqmax) {
-    if (nqmax <= 0) return 1;
-    // about 8 resident 128-thread CTAs on each of the 148 SMs
-    const int64_t target = 148 * 8;
-    int64_t spb = (nqmax * B + target - 1) / target;
-    return spb < 1 ? 1 : spb;
+// persistent CTAs of qdecode_mma on the current device: 2 per SM (its shared-memory ring allows two)
+int64_t persistent_ctas() {
+    static int cache[MAX_DEV] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEV) return 2 * 148;
+    if (!cache[dev]) {
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+        cache[dev] = sms;
+    }
+    return 2 * (int64_t)cache[dev];
 }
 
 int check_paged(const kv800_paged* P, const char* who) {
@@ -99,15 +182,36 @@ int check_paged(const kv800_paged* P, const char* who) {
     }
     return KV800_OK;
 }
+
+// Workspace plan of kv800_decode.  spb > 0: grid splits of spb sub-blocks (ns per row, the reference's sizing);
+// spb <= 0: persistent, G0 CTAs over the flattened sub-block list.  Layout: status word | prefix[B + 1] (persistent)
+// | MO, LO [nslots][16] | AO [nslots][16][128], each 256-byte aligned.
+struct Plan {
+    bool persistent;
+    int64_t ns, G0, nslots, prefix_off, mo_off, lo_off, ao_off, bytes;
+};
+
+int64_t up256(int64_t x) { return (x + 255) & ~(int64_t)255; }
+
+Plan make_plan(int64_t B, int64_t nqmax, int64_t win, int64_t spb) {
+    Plan p{};
+    const int64_t nq = win ? 0 : nqmax;
+    p.persistent = spb <= 0 && nq > 0;
+    p.ns = (nq > 0 && !p.persistent) ? (nq + spb - 1) / spb : 0;
+    p.G0 = p.persistent ? persistent_ctas() : 0;
+    p.nslots = p.persistent ? p.G0 + B + B * NX_DEFAULT : B * (p.ns + NX_DEFAULT);
+    p.prefix_off = 256;
+    p.mo_off = up256(p.prefix_off + (p.persistent ? (B + 1) * 8 : 0));
+    p.lo_off = up256(p.mo_off + p.nslots * QROWS * 4);
+    p.ao_off = up256(p.lo_off + p.nslots * QROWS * 4);
+    p.bytes = up256(p.ao_off + p.nslots * QROWS * DIM * 4);
+    return p;
+}
 }  // namespace
 
 extern "C" int64_t kv800_decode_workspace_size(int64_t B, int64_t nqmax, int64_t win, int64_t spb) {
     if (B < 0) return -1;
-    const int64_t nq = win ? 0 : nqmax;
-    if (spb <= 0) spb = choose_spb(B, nq);
-    const int64_t ns = nq > 0 ? (nq + spb - 1) / spb : 0;
-    const int64_t slots = ns + NX_DEFAULT;
-    return 256 + B * slots * QROWS * (int64_t)sizeof(float) * (2 + DIM) + 256;
+    return make_plan(B, nqmax, win, spb).bytes;
 }
 
 static int qdecode_setup() {
@@ -130,26 +234,6 @@ static int xdecode_setup() {
         done = 1;
     }
     return KV800_OK;
-}
-
-static int launch_decode_parts(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t, const uint16_t* sin_t,
-                               int64_t npos, int64_t B, int64_t ns, int64_t spb, int64_t nx, float* mo, float* lo,
-                               float* ao, int* status, cudaStream_t st, const char* who) {
-    const int nslots = (int)(ns + nx);
-    if (ns > 0) {
-        int rc0 = qdecode_setup();
-        if (rc0) return rc0;
-        QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
-                  mo, lo, ao, nslots, (int)spb, SCALE, status};
-        qdecode_mma<<<dim3((unsigned)B, (unsigned)ns), 128, QM_SMEM, st>>>(qa);
-        int rc = cuda_status(cudaGetLastError(), who);
-        if (rc) return rc;
-    }
-    int rcx = xdecode_setup();
-    if (rcx) return rcx;
-    XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, nslots, (int)ns, (int)nx, SCALE, status};
-    xdecode_mma<<<dim3((unsigned)B, (unsigned)nx), 128, XM_SMEM, st>>>(xa);
-    return cuda_status(cudaGetLastError(), who);
 }
 
 extern "C" int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t, const uint16_t* sin_t,
@@ -182,30 +266,66 @@ extern "C" int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint1
         set_error("kv800_decode: workspace must be 256-byte aligned");
         return KV800_ERR_ARG;
     }
-    const int64_t nq = P->win ? 0 : P->nqmax;
-    if (spb <= 0) spb = choose_spb(B, nq);
-    const int64_t ns = nq > 0 ? (nq + spb - 1) / spb : 0;
-    if (ns > 65535) {
-        set_error("kv800_decode: %lld splits above the grid limit (raise spb)", (long long)ns);
+    const Plan pl = make_plan(B, P->nqmax, P->win, spb);
+    if (pl.ns > 65535) {
+        set_error("kv800_decode: %lld splits above the grid limit (raise spb)", (long long)pl.ns);
         return KV800_ERR_RANGE;
     }
-    const int64_t need = kv800_decode_workspace_size(B, P->nqmax, P->win, spb);
-    if (workspace_bytes < need) {
-        set_error("kv800_decode: workspace of %lld bytes, %lld needed", (long long)workspace_bytes, (long long)need);
+    if (workspace_bytes < pl.bytes) {
+        set_error("kv800_decode: workspace of %lld bytes, %lld needed", (long long)workspace_bytes,
+                  (long long)pl.bytes);
         return KV800_ERR_RANGE;
     }
     cudaStream_t st = as_stream(stream);
     char* ws = static_cast<char*>(workspace);
     int* status = reinterpret_cast<int*>(ws);
-    const int64_t nslots = ns + NX_DEFAULT;
-    float* mo = reinterpret_cast<float*>(ws + 256);
-    float* lo = mo + B * nslots * QROWS;
-    float* ao = lo + B * nslots * QROWS;
+    int64_t* prefix = reinterpret_cast<int64_t*>(ws + pl.prefix_off);
+    float* mo = reinterpret_cast<float*>(ws + pl.mo_off);
+    float* lo = reinterpret_cast<float*>(ws + pl.lo_off);
+    float* ao = reinterpret_cast<float*>(ws + pl.ao_off);
     rc = cuda_status(cudaMemsetAsync(status, 0, sizeof(int), st), "kv800_decode status reset");
     if (rc) return rc;
-    rc = launch_decode_parts(P, q, cos_t, sin_t, npos, B, ns, spb, NX_DEFAULT, mo, lo, ao, status, st, "kv800_decode");
+    SlotMap sm{};
+    sm.nx = NX_DEFAULT;
+    if (pl.persistent) {
+        rc = qdecode_setup();
+        if (rc) return rc;
+        qsched_kernel<<<1, 1024, 0, st>>>(P->NQ, P->nqmax, B, prefix);
+        rc = cuda_status(cudaGetLastError(), "kv800_decode schedule");
+        if (rc) return rc;
+        QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
+                  mo, lo, ao, 0, 0, SCALE, status, prefix, B};
+        qdecode_mma<<<(unsigned)pl.G0, 128, QM_SMEM, st>>>(qa);
+        rc = cuda_status(cudaGetLastError(), "kv800_decode qdecode");
+        if (rc) return rc;
+        sm.prefix = prefix;
+        sm.B = B;
+        sm.G0 = pl.G0;
+        sm.xbase = pl.G0 + B;
+        sm.xstride = NX_DEFAULT;
+    } else {
+        const int64_t rowslots = pl.ns + NX_DEFAULT;
+        if (pl.ns > 0) {
+            rc = qdecode_setup();
+            if (rc) return rc;
+            QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
+                      mo, lo, ao, (int)rowslots, (int)spb, SCALE, status, nullptr, B};
+            qdecode_mma<<<dim3((unsigned)B, (unsigned)pl.ns), 128, QM_SMEM, st>>>(qa);
+            rc = cuda_status(cudaGetLastError(), "kv800_decode qdecode");
+            if (rc) return rc;
+        }
+        sm.ns = (int)pl.ns;
+        sm.qstride = rowslots;
+        sm.xbase = pl.ns;
+        sm.xstride = rowslots;
+    }
+    rc = xdecode_setup();
     if (rc) return rc;
-    combine_kernel<<<(unsigned)B, 512, 0, st>>>(mo, lo, ao, (int)ns, (int)nslots, out);
+    XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, sm.xbase, sm.xstride, NX_DEFAULT, SCALE, status};
+    xdecode_mma<<<dim3((unsigned)B, (unsigned)NX_DEFAULT), 128, XM_SMEM, st>>>(xa);
+    rc = cuda_status(cudaGetLastError(), "kv800_decode xdecode");
+    if (rc) return rc;
+    combine_kernel<<<(unsigned)B, 512, 0, st>>>(mo, lo, ao, sm, out);
     return cuda_status(cudaGetLastError(), "kv800_decode combine");
 }
 
@@ -233,7 +353,7 @@ extern "C" int kv800_qdecode(const uint16_t* q, const uint8_t* qpool, int64_t qp
     int rc0 = qdecode_setup();
     if (rc0) return rc0;
     QMArgs qa{q, qpool, qpool_bytes, boff, boff_stride, NQ, nqmax, cos_t, sin_t, npos,
-              mo, lo, ao, (int)(ns + 1), (int)spb, scale, status};
+              mo, lo, ao, (int)(ns + 1), (int)spb, scale, status, nullptr, B};
     qdecode_mma<<<dim3((unsigned)B, (unsigned)ns), 128, QM_SMEM, as_stream(stream)>>>(qa);
     return cuda_status(cudaGetLastError(), "kv800_qdecode launch");
 }
@@ -262,7 +382,7 @@ extern "C" int kv800_xdecode(const uint16_t* q, const kv800_paged* P, const uint
     }
     int rcx = xdecode_setup();
     if (rcx) return rcx;
-    XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, (int)(ns + 1), (int)ns, 1, scale, status};
+    XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, ns, ns + 1, 1, scale, status};
     xdecode_mma<<<dim3((unsigned)B, 1), 128, XM_SMEM, as_stream(stream)>>>(xa);
     return cuda_status(cudaGetLastError(), "kv800_xdecode launch");
 }
@@ -282,6 +402,12 @@ extern "C" int kv800_combine(const float* mo, const float* lo, const float* ao, 
         set_error("kv800_combine: ao must be 16-byte and out 8-byte aligned");
         return KV800_ERR_ARG;
     }
-    combine_kernel<<<(unsigned)B, 512, 0, as_stream(stream)>>>(mo, lo, ao, (int)ns, (int)(ns + 1), out);
+    SlotMap sm{};
+    sm.ns = (int)ns;
+    sm.qstride = ns + 1;
+    sm.xbase = ns;
+    sm.xstride = ns + 1;
+    sm.nx = 1;
+    combine_kernel<<<(unsigned)B, 512, 0, as_stream(stream)>>>(mo, lo, ao, sm, out);
     return cuda_status(cudaGetLastError(), "kv800_combine launch");
 }

@@ -34,10 +34,15 @@ struct QMArgs {
     float* mo;
     float* lo;
     float* ao;
-    int nslots;
-    int spb;
+    int nslots;   // grid mode: slots per row (partial of split s of row b at slot b * nslots + s)
+    int spb;      // grid mode: sub-blocks per split
     float scale;
     int* status;
+    // persistent mode (prefix != nullptr): CTA c of G = min(gridDim.x, W) takes the flattened units
+    // [c W / G, (c + 1) W / G) of the rows' sub-block lists (prefix[b] = sum of min(NQ, nqmax) over rows < b,
+    // prefix[B] = W) and writes the partial of its segment of row b at slot c + b.
+    const int64_t* prefix;
+    int64_t B;
 };
 
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t orv) { return (a & mask) | orv; }
@@ -236,18 +241,63 @@ __global__ void __launch_bounds__(128, 2) qdecode_mma(QMArgs a) {
     uint32_t* cst = reinterpret_cast<uint32_t*>(smem + 2 * QM_STAGE);
     float2* vsl = reinterpret_cast<float2*>(smem + 2 * QM_STAGE + QM_CST_BYTES);
 
-    const int b = blockIdx.x, s = blockIdx.y, tid = threadIdx.x;
+    const int tid = threadIdx.x;
     const int h = tid >> 5, lane = tid & 31, g = lane >> 2, tig = lane & 3;
-    int64_t nq = a.NQ[b];
-    if (nq > a.nqmax) nq = a.nqmax;
-    const int64_t j0 = (int64_t)s * a.spb;
-    const int64_t j1 = min(j0 + a.spb, nq);
-    const int n = (int)max((int64_t)0, j1 - j0);
 
-    // ---- QK B fragments (q is bf16 already): column n = g is query row r = g of this head, zero for g >= 4
+    // ---- schedule: this CTA's units [u0, u1) and the row cursor of unit u0
+    int64_t u0, u1;          // units of this CTA
+    int b0;                  // row of unit u0
+    int64_t rs0, re0;        // global unit range of row b0 ([rs0, re0); grid mode: [0, nq))
+    int slot_c;              // grid mode: slot = b * nslots + slot_c; persistent: slot = slot_c + b
+    const bool persistent = a.prefix != nullptr;
+    if (!persistent) {
+        b0 = blockIdx.x;
+        const int s = blockIdx.y;
+        int64_t nq = a.NQ[b0];
+        if (nq > a.nqmax) nq = a.nqmax;
+        if (nq < 0) nq = 0;
+        u0 = min((int64_t)s * a.spb, nq);
+        u1 = min(u0 + a.spb, nq);
+        rs0 = 0;
+        re0 = nq;
+        slot_c = s;
+    } else {
+        const int64_t W = a.prefix[a.B];
+        const int64_t G = min((int64_t)gridDim.x, W);
+        const int64_t c = blockIdx.x;
+        if (c >= G) return;
+        u0 = c * W / G;
+        u1 = (c + 1) * W / G;
+        // largest b with prefix[b] <= u0 and a nonempty row (prefix[b + 1] > u0)
+        int64_t lo_b = 0, hi_b = a.B - 1;
+        while (lo_b < hi_b) {
+            const int64_t mid = (lo_b + hi_b + 1) >> 1;
+            if (a.prefix[mid] <= u0) lo_b = mid; else hi_b = mid - 1;
+        }
+        b0 = (int)lo_b;
+        rs0 = a.prefix[b0];
+        re0 = a.prefix[b0 + 1];
+        slot_c = (int)c;
+    }
+    const int n = (int)(u1 - u0);
+    // unit i (0 <= i < n) -> (row, sub-block) through a forward-only cursor
+    struct Cursor {
+        int b;
+        int64_t rs, re;
+    };
+    auto advance = [&](Cursor& cu, int64_t u) {
+        while (u >= cu.re) {
+            cu.b++;
+            cu.rs = cu.re;
+            cu.re = a.prefix[cu.b + 1];
+        }
+    };
+    Cursor cur{b0, rs0, re0}, pre{b0, rs0, re0};
+
+    // ---- QK B fragments of row `row` (q is bf16 already): column n = g is query row r = g of this head, 0 for g >= 4
     uint32_t bq[8][2];
-    {
-        const uint16_t* qr = a.q + ((int64_t)b * QROWS + h * 4 + (g & 3)) * DIM;
+    auto load_q = [&](int row) {
+        const uint16_t* qr = a.q + ((int64_t)row * QROWS + h * 4 + (g & 3)) * DIM;
 #pragma unroll
         for (int ks = 0; ks < 8; ks++)
 #pragma unroll
@@ -257,12 +307,17 @@ __global__ void __launch_bounds__(128, 2) qdecode_mma(QMArgs a) {
                 const uint32_t v = (uint32_t)qr[d0] | ((uint32_t)qr[d1] << 16);
                 bq[ks][hl] = (g < 4) ? v : 0u;
             }
-    }
+    };
+    int qrow = b0;
+    load_q(qrow);
     // ---- prologue: sub-blocks 0 and 1 of this split into the two stages
 #pragma unroll
     for (int i = 0; i < 2; i++) {
         const uint8_t* src;
-        if (i < n && sub_ok(a, b, j0 + i, src)) stage_subblock(raw0 + i * QM_STAGE, src, tid);
+        if (i < n) {
+            if (persistent) advance(pre, u0 + i);
+            if (sub_ok(a, pre.b, u0 + i - pre.rs, src)) stage_subblock(raw0 + i * QM_STAGE, src, tid);
+        }
         cp_commit();
     }
 
@@ -287,8 +342,62 @@ __global__ void __launch_bounds__(128, 2) qdecode_mma(QMArgs a) {
 #pragma unroll
         for (int e = 0; e < 4; e++) acc[i][e] = 0.f;
 
+    // write the partial (m, l, acc + lv) of the current segment to `slot` and reset the accumulators
+    auto flush_partial = [&](int64_t slot) {
+        float l[2], lv[2];
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            float x = l_part[rr], y = lv_part[rr];
+            x += __shfl_xor_sync(0xffffffffu, x, 4);
+            x += __shfl_xor_sync(0xffffffffu, x, 8);
+            x += __shfl_xor_sync(0xffffffffu, x, 16);
+            y += __shfl_xor_sync(0xffffffffu, y, 4);
+            y += __shfl_xor_sync(0xffffffffu, y, 8);
+            y += __shfl_xor_sync(0xffffffffu, y, 16);
+            l[rr] = x;
+            lv[rr] = y;
+        }
+        if (tig < 2) {
+#pragma unroll
+            for (int rr = 0; rr < 2; rr++) {
+                const int r = 2 * tig + rr;
+                const int64_t row = slot * QROWS + h * 4 + r;
+                if (g == 0) {
+                    a.mo[row] = m[rr];
+                    a.lo[row] = l[rr];
+                }
+                float* o = a.ao + row * DIM;
+#pragma unroll
+                for (int i0 = 0; i0 < 8; i0++) {
+                    const float f = __uint_as_float((uint32_t)(135 - i0) << 23);   // 2^(8 - i0)
+                    o[2 * g + 16 * i0] = fmaf(acc[i0][rr] - acc[8][rr], f, lv[rr]);
+                    o[2 * g + 1 + 16 * i0] = fmaf(acc[i0][rr + 2] - acc[8][rr + 2], f, lv[rr]);
+                }
+            }
+        }
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            m[rr] = -1e30f;
+            l_part[rr] = lv_part[rr] = 0.f;
+        }
+#pragma unroll
+        for (int i9 = 0; i9 < 9; i9++)
+#pragma unroll
+            for (int e9 = 0; e9 < 4; e9++) acc[i9][e9] = 0.f;
+    };
+    auto slot_of = [&](int row) -> int64_t {
+        return persistent ? (int64_t)slot_c + row : (int64_t)row * a.nslots + slot_c;
+    };
+
     for (int i = 0; i < n; i++) {
-        const int64_t jb = j0 + i;
+        if (persistent) advance(cur, u0 + i);
+        if (cur.b != qrow) {                 // segment boundary: the previous row's partial is complete
+            flush_partial(slot_of(qrow));
+            qrow = cur.b;
+            load_q(qrow);
+        }
+        const int b = cur.b;
+        const int64_t jb = u0 + i - cur.rs;
         const uint8_t* src;
         const bool ok = sub_ok(a, b, jb, src);
         uint8_t* raw = raw0 + (i & 1) * QM_STAGE;
@@ -441,44 +550,14 @@ __global__ void __launch_bounds__(128, 2) qdecode_mma(QMArgs a) {
         __syncthreads();   // stage (i & 1) and cst / vsl free again
         if (i + 2 < n) {
             const uint8_t* src2;
-            if (sub_ok(a, b, jb + 2, src2)) stage_subblock(raw, src2, tid);
+            if (persistent) advance(pre, u0 + i + 2);
+            if (sub_ok(a, pre.b, u0 + i + 2 - pre.rs, src2)) stage_subblock(raw, src2, tid);
         }
         cp_commit();
     }
     cp_wait<0>();
-    // ---- finalize: rows r = 2 tig, 2 tig + 1 (valid for tig < 2)
-    float l[2], lv[2];
-#pragma unroll
-    for (int rr = 0; rr < 2; rr++) {
-        float x = l_part[rr], y = lv_part[rr];
-        x += __shfl_xor_sync(0xffffffffu, x, 4);
-        x += __shfl_xor_sync(0xffffffffu, x, 8);
-        x += __shfl_xor_sync(0xffffffffu, x, 16);
-        y += __shfl_xor_sync(0xffffffffu, y, 4);
-        y += __shfl_xor_sync(0xffffffffu, y, 8);
-        y += __shfl_xor_sync(0xffffffffu, y, 16);
-        l[rr] = x;
-        lv[rr] = y;
-    }
-    if (tig < 2) {
-        const int64_t slot = (int64_t)b * a.nslots + s;
-#pragma unroll
-        for (int rr = 0; rr < 2; rr++) {
-            const int r = 2 * tig + rr;
-            const int64_t row = slot * QROWS + h * 4 + r;
-            if (g == 0) {
-                a.mo[row] = m[rr];
-                a.lo[row] = l[rr];
-            }
-            float* o = a.ao + row * DIM;
-#pragma unroll
-            for (int i0 = 0; i0 < 8; i0++) {
-                const float f = __uint_as_float((uint32_t)(135 - i0) << 23);   // 2^(8 - i0)
-                o[2 * g + 16 * i0] = fmaf(acc[i0][rr] - acc[8][rr], f, lv[rr]);
-                o[2 * g + 1 + 16 * i0] = fmaf(acc[i0][rr + 2] - acc[8][rr + 2], f, lv[rr]);
-            }
-        }
-    }
+    flush_partial(slot_of(qrow));
 }
+
 
 }  // namespace kv800

@@ -11,7 +11,7 @@
 //   PV       A = V^T via ldmatrix.x4.trans (dims on M, tokens on K), B = P transposed from the QK accumulator with
 //            movmatrix, split into bf16 hi + lo (P - hi) so the products keep ~16 bits of P; fp32 accumulate.
 // Online softmax in the log2 domain with a lazily moved reference point (as in qdecode_mma).  The partial (m, l, acc)
-// goes to slot slot0 + e of the reference's layout (kv800.py:224-228 for the single-split form).
+// goes to slot xbase + b xstride + e (the reference's slot ns of row b for the single-split form, kv800.py:224-228).
 #pragma once
 #include "qdecode_mma.cuh"
 
@@ -26,8 +26,8 @@ struct XMArgs {
     float* mo;
     float* lo;
     float* ao;
-    int nslots;
-    int slot0;
+    int64_t xbase;     // partial of split e of row b at slot xbase + b * xstride + e
+    int64_t xstride;
     int nx;
     float scale;
     int* status;
@@ -286,7 +286,7 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
         l[rr] = x;
     }
     if (tig < 2) {
-        const int64_t slot = (int64_t)b * a.nslots + a.slot0 + e;
+        const int64_t slot = a.xbase + (int64_t)b * a.xstride + e;
 #pragma unroll
         for (int rr = 0; rr < 2; rr++) {
             const int64_t row = slot * QROWS + h * 4 + 2 * tig + rr;

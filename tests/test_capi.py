@@ -62,11 +62,22 @@ def test_host_argument_checks():
     assert L.kv800_check_status(None, None, None) == _lib.ERR_ARG
 
 
-@pytest.mark.parametrize("B,nqmax,win", [(64, 127, 0), (4, 7, 0), (64, 0, 256), (2048, 127, 0)])
-def test_workspace_size(B, nqmax, win):
+def _plan_bytes(B, nqmax, win, spb, G0=296):
+    up = lambda x: (x + 255) & ~255
+    nq = 0 if win else nqmax
+    persistent = spb <= 0 and nq > 0
+    ns = 0 if (nq == 0 or persistent) else -(-nq // spb)
+    nslots = (G0 + B + 4 * B) if persistent else B * (ns + 4)
+    mo = up(256 + ((B + 1) * 8 if persistent else 0))
+    lo = up(mo + nslots * 64)
+    ao = up(lo + nslots * 64)
+    return up(ao + nslots * 16 * 128 * 4)
+
+
+@pytest.mark.parametrize("B,nqmax,win,spb", [(64, 127, 0, 0), (4, 7, 0, 0), (64, 0, 256, 0), (2048, 127, 0, 0),
+                                             (2, 19, 0, 3), (64, 127, 0, 7)])
+def test_workspace_size(B, nqmax, win, spb):
+    """Workspace plan: status word, schedule prefix (persistent), MO / LO / AO partials (no GPU: the persistent CTA
+    count falls back to 2 x 148 when no device answers)."""
     L = _lib.lib()
-    ws = L.kv800_decode_workspace_size(B, nqmax, win, 0)
-    assert ws >= 256 + B * 16 * 130 * 4 * 4
-    spb = max(1, -(-nqmax * B // (148 * 8))) if (nqmax and not win) else 1
-    ns = -(-nqmax // spb) if (nqmax and not win) else 0
-    assert ws == 256 + B * (ns + 4) * 16 * 4 * 130 + 256
+    assert L.kv800_decode_workspace_size(B, nqmax, win, spb) == _plan_bytes(B, nqmax, win, spb)

@@ -1,0 +1,110 @@
+"""Ragged batches through the decode (BASELINE config 4 in small): rows of different lengths, including an empty row
+and rows without quantized sub-blocks, with sub-blocks and exact pages at shuffled pool slots.  The pools are built
+on the host with the oracle's quantizer and decoded by both the CUDA path (persistent schedule and explicit split
+sizes) and the oracle; the outputs must agree within the decode tolerance."""
+import numpy as np
+import pytest
+import torch
+
+import inputs as I
+from _util import assert_parity, nb, tb
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+EBS = 64
+
+
+def build(lengths, win, seed, distinct=None):
+    """Host pools for rows of `lengths`; `distinct` = quantize only that many different sub-blocks and scatter them
+    at random over the rows' tables (the quantized part need not match the exact pages)."""
+    rs = np.random.RandomState(seed)
+    B = len(lengths)
+    nqs = [0 if win else max(0, n - 128) // 256 for n in lengths]
+    nslot = sum(nqs) + 5
+    slots = rs.permutation(nslot)
+    qpool = np.zeros((nslot, 51200), np.uint8)
+    maxpg = max(lengths) // EBS + 2
+    boff = np.zeros((B, max(1, max(nqs))), np.int64)
+    eoff = np.zeros((B, maxpg), np.int64)
+    npages = sum(maxpg for _ in lengths) + 3
+    pages = rs.permutation(npages)
+    epool = np.zeros((npages, 4, EBS, 256), np.uint16)
+    K_all = [I.f32_to_bf16(rs.standard_normal((n, 4, 128)).astype(np.float32) +
+                           2 * rs.standard_normal((1, 4, 128)).astype(np.float32)) for n in lengths]
+    V_all = [I.f32_to_bf16(rs.standard_normal((n, 4, 128)).astype(np.float32)) for n in lengths]
+    # all full sub-blocks in one oracle call, placed at the shuffled slots
+    if distinct:
+        k, v = I.quant_inputs("parity", distinct, seed=seed)
+        pool = O.quantize_blocks(k, v)
+        sbs = pool[rs.randint(0, distinct, sum(nqs))]
+    else:
+        ks = [K_all[b][256 * j:256 * j + 256] for b in range(B) for j in range(nqs[b])]
+        vs = [V_all[b][256 * j:256 * j + 256] for b in range(B) for j in range(nqs[b])]
+        sbs = O.quantize_blocks(np.stack(ks), np.stack(vs)) if ks else None
+    if sum(nqs):
+        si = 0
+        for b in range(B):
+            for j in range(nqs[b]):
+                qpool[slots[si]] = sbs[si]
+                boff[b, j] = slots[si] * 51200
+                si += 1
+    pi = 0
+    for b, n in enumerate(lengths):
+        npg = n // EBS + 1
+        eoff[b, :npg] = pages[pi:pi + npg] * 4 * EBS * 256
+        pi += npg
+        if n:
+            t = np.arange(n)
+            pg = eoff[b, t // EBS] // (4 * EBS * 256)
+            epool[pg, :, t % EBS, :128] = K_all[b]
+            epool[pg, :, t % EBS, 128:] = V_all[b]
+    sk = np.zeros((B, 4, 4, 128), np.uint16)
+    for b, n in enumerate(lengths):
+        m = min(4, n)
+        sk[b, :m] = K_all[b][:m]
+    sv = np.zeros_like(sk)
+    for b, n in enumerate(lengths):
+        m = min(4, n)
+        sv[b, :m] = V_all[b][:m]
+    q = I.f32_to_bf16(2 * rs.standard_normal((B, 16, 128)).astype(np.float32))
+    P = dict(qpool=qpool, boff=boff, epool=epool, eoff=eoff, ebs=EBS, e_hs=EBS * 256, e_ts=256, e_v=128,
+             sk=sk if win else None, sv=sv if win else None, skoff=np.arange(B, dtype=np.int64) * 2048,
+             svoff=np.arange(B, dtype=np.int64) * 2048, N=np.array(lengths, np.int32), NQ=np.array(nqs, np.int32),
+             nqmax=max(nqs), win=win)
+    return P, q
+
+
+def to_dev(kv800, P):
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(DEV)
+    return kv800.Paged(qpool=t(P["qpool"]), boff=t(P["boff"]), epool=tb(P["epool"], DEV), eoff=t(P["eoff"]),
+                       ebs=P["ebs"], e_hs=P["e_hs"], e_ts=P["e_ts"], e_v=P["e_v"],
+                       sk=None if P["sk"] is None else tb(P["sk"], DEV),
+                       sv=None if P["sv"] is None else tb(P["sv"], DEV), skoff=t(P["skoff"]), svoff=t(P["svoff"]),
+                       N=t(P["N"]), NQ=t(P["NQ"]), nqmax=P["nqmax"], win=P["win"])
+
+
+LENGTHS = [0, 3, 383, 384, 900, 2000, 5000, 1, 640]
+
+
+@pytest.mark.parametrize("win", [0, 256])
+@pytest.mark.parametrize("spb", [None, 1, 4])
+def test_ragged_vs_oracle(win, spb):
+    from lfm3_kv800 import kv800
+    P, q = build(LENGTHS, win, seed=17 + win)
+    cs, sn = I.rope_tables(5200)
+    out = kv800.decode(to_dev(kv800, P), tb(q, DEV), tb(cs, DEV), tb(sn, DEV), spb=spb)
+    ref = O.decode(P, q, cs, sn)
+    got = nb(out)
+    assert_parity(got, ref, f"ragged win={win} spb={spb}")
+    assert np.all(got[0] == 0), "the empty row must decode to zeros"
+
+
+def test_persistent_many_rows():
+    """More rows than persistent CTAs with tiny sub-block lists: every CTA range crosses several rows."""
+    from lfm3_kv800 import kv800
+    lengths = [384 + 256 * (i % 3) for i in range(400)]
+    P, q = build(lengths, 0, seed=5, distinct=24)
+    cs, sn = I.rope_tables(1200)
+    out = kv800.decode(to_dev(kv800, P), tb(q, DEV), tb(cs, DEV), tb(sn, DEV))
+    assert_parity(nb(out), O.decode(P, q, cs, sn), "400 short rows")
