@@ -27,12 +27,23 @@ def build(lengths, win, seed, distinct=None):
     maxpg = max(lengths) // EBS + 2
     boff = np.zeros((B, max(1, max(nqs))), np.int64)
     eoff = np.zeros((B, maxpg), np.int64)
-    npages = sum(maxpg for _ in lengths) + 3
+    npages = sum(n // EBS + 1 for n in lengths) + 3
     pages = rs.permutation(npages)
     epool = np.zeros((npages, 4, EBS, 256), np.uint16)
-    K_all = [I.f32_to_bf16(rs.standard_normal((n, 4, 128)).astype(np.float32) +
-                           2 * rs.standard_normal((1, 4, 128)).astype(np.float32)) for n in lengths]
-    V_all = [I.f32_to_bf16(rs.standard_normal((n, 4, 128)).astype(np.float32)) for n in lengths]
+    # token data: every position when the sub-blocks are built from it, else only what the decode reads (the exact
+    # positions [256 nq, n) and the 4 sink positions); other positions stay zero
+    K_all, V_all = [], []
+    for b, n in enumerate(lengths):
+        lo = 0 if not distinct else 256 * nqs[b]
+        K = np.zeros((n, 4, 128), np.uint16)
+        V = np.zeros((n, 4, 128), np.uint16)
+        for a_, z_ in ((0, min(4, n)), (lo, n)):
+            if z_ > a_:
+                K[a_:z_] = I.f32_to_bf16(rs.standard_normal((z_ - a_, 4, 128)).astype(np.float32) +
+                                        2 * rs.standard_normal((1, 4, 128)).astype(np.float32))
+                V[a_:z_] = I.f32_to_bf16(rs.standard_normal((z_ - a_, 4, 128)).astype(np.float32))
+        K_all.append(K)
+        V_all.append(V)
     # all full sub-blocks in one oracle call, placed at the shuffled slots
     if distinct:
         k, v = I.quant_inputs("parity", distinct, seed=seed)
