@@ -293,6 +293,7 @@ def main():
     # ---- end to end through the public API with host buffers
     e2e = None
     if not a.no_e2e:
+        B = a.seqs
         nl = len(layers)
         hq = [q.cpu().pin_memory() for q in qs]
         hk = torch.randn(nl, B, 4, 128).to(torch.bfloat16).pin_memory()
