@@ -150,17 +150,17 @@ constexpr int NX_DEFAULT = 4;                   // exact splits per row in kv800
 constexpr float SCALE = 0.12751743074602467f;   // 128^-0.5 * log2(e)
 constexpr int MAX_DEV = 64;
 
-// persistent CTAs of qdecode_mma on the current device: 2 per SM (its shared-memory ring allows two)
+// persistent CTAs of qdecode_mma on the current device: 3 per SM (its registers and shared-memory ring allow three)
 int64_t persistent_ctas() {
     static int cache[MAX_DEV] = {0};
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEV) return 2 * 148;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEV) return 3 * 148;
     if (!cache[dev]) {
         int sms = 0;
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
         cache[dev] = sms;
     }
-    return 2 * (int64_t)cache[dev];
+    return 3 * (int64_t)cache[dev];
 }
 
 int check_paged(const kv800_paged* P, const char* who) {

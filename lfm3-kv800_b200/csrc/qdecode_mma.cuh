@@ -87,6 +87,13 @@ __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1,
                  : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// 2^x with the hardware approximation (relative error ~2^-22); arguments here are <= 6 (log2 domain, lazily moved
+// max), and results below 2^-126 flush to 0, which drops nothing a softmax weight needs.
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
@@ -193,27 +200,41 @@ __device__ __forceinline__ void token_regs(uint32_t w0, uint32_t w1, const uint4
 // kc region: token row t (128 B = 8 chunks): chunk c stored at c ^ (t & 7).  vb region: 128-B line L (2 tokens):
 // chunk c stored at c ^ (L & 7).  A warp's fragment loads (8 tokens x one 8- or 2-byte piece of the same head) then
 // hit 8 different bank groups.  Scale region linear.
-constexpr int QM_STAGE = SUB;                        // raw bytes per stage
+// Stage unit = half a sub-block: the kc rows and vb lines of 128 tokens (+ the 2 KB scale region with the first half).
+constexpr int QM_HALF = BLK / 2;
+constexpr int QM_KC_BYTES = QM_HALF * 128;           // 16 KB of kc rows
+constexpr int QM_VB_BYTES = QM_HALF * 64;            // 8 KB of vb lines
+constexpr int QM_SC_BYTES = SUB - VLO_O;             // vlo | vsc | klo | ksc, 2 KB
+constexpr int ST_VB = QM_KC_BYTES, ST_SC = QM_KC_BYTES + QM_VB_BYTES;
+constexpr int QM_STAGE = QM_KC_BYTES + QM_VB_BYTES + QM_SC_BYTES;   // 26,624 B
 constexpr int QM_CST_BYTES = HEADS * 4 * 4 * 4 * 8;  // [h][plane][tig][pair] x (A, L) bf16x2
 constexpr int QM_VSL_BYTES = BLK * 2 * 8;            // [t][group] x (vl, vs) fp32
-constexpr int QM_SMEM = 2 * QM_STAGE + QM_CST_BYTES + QM_VSL_BYTES;
+constexpr int QM_SMEM = 2 * QM_STAGE + QM_CST_BYTES + QM_VSL_BYTES;   // 59,392 B: three CTAs per SM
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-__device__ __forceinline__ int swz_chunk(int c) {            // chunk index c of a 51,200-B sub-block -> smem chunk
-    if (c < 2048) return (c & ~7) | ((c & 7) ^ ((c >> 3) & 7));
-    if (c < 3072) {
-        const int r = c - 2048;
-        return 2048 + ((r & ~7) | ((r & 7) ^ ((r >> 3) & 7)));
-    }
-    return c;
-}
+// 16-byte chunk c of a 128-B row / line r (local to the half) -> its swizzled chunk
+__device__ __forceinline__ int swz(int c) { return (c & ~7) | ((c & 7) ^ ((c >> 3) & 7)); }
 
-__device__ __forceinline__ void stage_subblock(uint8_t* dst, const uint8_t* src, int tid) {
+// copy half `half` of the sub-block at src into a stage: kc rows, vb lines (both swizzled), and for half 0 the scales
+__device__ __forceinline__ void stage_half(uint8_t* dst, const uint8_t* src, int half, int tid) {
     const uint32_t d0 = smem_u32(dst);
-    for (int c = tid; c < SUB / 16; c += 128) {
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d0 + 16 * swz_chunk(c)), "l"(src + 16 * c)
-                     : "memory");
+    const int nck = QM_KC_BYTES / 16, ncv = QM_VB_BYTES / 16, ncs = half ? 0 : QM_SC_BYTES / 16;
+    for (int c = tid; c < nck + ncv + ncs; c += 128) {
+        int so, dof;
+        if (c < nck) {
+            so = half * QM_KC_BYTES + 16 * c;
+            dof = 16 * swz(c);
+        } else if (c < nck + ncv) {
+            const int r = c - nck;
+            so = VB_O + half * QM_VB_BYTES + 16 * r;
+            dof = ST_VB + 16 * swz(r);
+        } else {
+            const int r = c - nck - ncv;
+            so = VLO_O + 16 * r;
+            dof = ST_SC + 16 * r;
+        }
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d0 + dof), "l"(src + so) : "memory");
     }
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
@@ -235,7 +256,7 @@ __device__ __forceinline__ bool sub_ok(const QMArgs& a, int b, int64_t jb, const
            (jb + 1) * BLK <= a.npos;
 }
 
-__global__ void __launch_bounds__(128, 2) qdecode_mma(QMArgs a) {
+__global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* raw0 = smem;
     uint32_t* cst = reinterpret_cast<uint32_t*>(smem + 2 * QM_STAGE);
@@ -311,14 +332,15 @@ __global__ void __launch_bounds__(128, 2) qdecode_mma(QMArgs a) {
     int qrow = b0;
     load_q(qrow);
     // ---- prologue: sub-blocks 0 and 1 of this split into the two stages
-#pragma unroll
-    for (int i = 0; i < 2; i++) {
+    // ---- prologue: both halves of the first sub-block into the two stages
+    {
         const uint8_t* src;
-        if (i < n) {
-            if (persistent) advance(pre, u0 + i);
-            if (sub_ok(a, pre.b, u0 + i - pre.rs, src)) stage_subblock(raw0 + i * QM_STAGE, src, tid);
+        const bool ok0 = n > 0 && sub_ok(a, pre.b, u0 - pre.rs, src);
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            if (ok0) stage_half(raw0 + k * QM_STAGE, src, k, tid);
+            cp_commit();
         }
-        cp_commit();
     }
 
     // per-thread shared-memory offsets inside a 16-token tile starting at a multiple of 16 (the swizzle phase
@@ -331,7 +353,7 @@ __global__ void __launch_bounds__(128, 2) qdecode_mma(QMArgs a) {
     for (int q4 = 0; q4 < 4; q4++) {
         const int L = tig + 4 * (q4 >> 1);                               // line of token t0 + 2tig + (q4&1) + 8(q4>>1)
         const int cc = (q4 & 1) * 4 + h;
-        voff[q4] = VB_O + L * 128 + ((cc ^ L) << 4) + 2 * g;
+        voff[q4] = ST_VB + L * 128 + ((cc ^ L) << 4) + 2 * g;
     }
     const int vsl_a = 2 * g + (h >> 1), vsl_b = 2 * (g + 8) + (h >> 1);
 
@@ -389,50 +411,59 @@ __global__ void __launch_bounds__(128, 2) qdecode_mma(QMArgs a) {
         return persistent ? (int64_t)slot_c + row : (int64_t)row * a.nslots + slot_c;
     };
 
-    for (int i = 0; i < n; i++) {
-        if (persistent) advance(cur, u0 + i);
-        if (cur.b != qrow) {                 // segment boundary: the previous row's partial is complete
-            flush_partial(slot_of(qrow));
-            qrow = cur.b;
-            load_q(qrow);
+    int b = 0;
+    int64_t jb = 0;
+    bool ok = false;
+    for (int k = 0; k < 2 * n; k++) {
+        const int i = k >> 1, half = k & 1;
+        if (half == 0) {
+            if (persistent) advance(cur, u0 + i);
+            if (cur.b != qrow) {                 // segment boundary: the previous row's partial is complete
+                flush_partial(slot_of(qrow));
+                qrow = cur.b;
+                load_q(qrow);
+            }
+            b = cur.b;
+            jb = u0 + i - cur.rs;
+            const uint8_t* src;
+            ok = sub_ok(a, b, jb, src);
         }
-        const int b = cur.b;
-        const int64_t jb = u0 + i - cur.rs;
-        const uint8_t* src;
-        const bool ok = sub_ok(a, b, jb, src);
-        uint8_t* raw = raw0 + (i & 1) * QM_STAGE;
+        uint8_t* raw = raw0 + (k & 1) * QM_STAGE;
         cp_wait<1>();
         __syncthreads();
-        if (!ok) {
-            if (tid == 0) flag(a.status, (jb >= a.boff_stride || (jb + 1) * BLK > a.npos) ? ST_TABLE : ST_QPOOL);
-        } else {
-            // ---- cooperative preprocessing: dequant constants and (vl, vs) of this sub-block
-            const float pws[4] = {32.f, 8.f, 2.f, 8.f};   // 2^(5 - 2p); plane 3 is encoded like plane 1
+        if (half == 0) {
+            if (!ok) {
+                if (tid == 0) flag(a.status, (jb >= a.boff_stride || (jb + 1) * BLK > a.npos) ? ST_TABLE : ST_QPOOL);
+            } else {
+                // ---- cooperative preprocessing: dequant constants and (vl, vs) of this sub-block
+                const float pws[4] = {32.f, 8.f, 2.f, 8.f};   // 2^(5 - 2p); plane 3 is encoded like plane 1
 #pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const int idx = tid + 128 * e;             // (hh, p, tg, pi)
-                const int pi = idx & 3, tg = (idx >> 2) & 3, p = (idx >> 4) & 3, hh = idx >> 6;
-                const int j = 8 * tg + ((pi & 1) | ((pi & 2) << 1));
-                const uint8_t* sc = raw + KSC_O + hh * DIM + 32 * p + j;
-                const uint8_t* lo = raw + KLO_O + hh * DIM + 32 * p + j;
-                float s0, s1, l0, l1;
-                e4m3x2_to_f32((uint32_t)sc[0] | ((uint32_t)sc[2] << 8), s0, s1);
-                e4m3x2_to_f32((uint32_t)lo[0] | ((uint32_t)lo[2] << 8), l0, l1);
-                const float pw = (p == 0) ? pws[0] : (p == 2) ? pws[2] : pws[1];
-                cst[2 * idx] = pack_bf16(s0 * pw, s1 * pw);
-                cst[2 * idx + 1] = pack_bf16(l0, l1);
-            }
+                for (int e = 0; e < 2; e++) {
+                    const int idx = tid + 128 * e;             // (hh, p, tg, pi)
+                    const int pi = idx & 3, tg = (idx >> 2) & 3, p = (idx >> 4) & 3, hh = idx >> 6;
+                    const int j = 8 * tg + ((pi & 1) | ((pi & 2) << 1));
+                    const uint8_t* sc = raw + ST_SC + (KSC_O - VLO_O) + hh * DIM + 32 * p + j;
+                    const uint8_t* lo = raw + ST_SC + (KLO_O - VLO_O) + hh * DIM + 32 * p + j;
+                    float s0, s1, l0, l1;
+                    e4m3x2_to_f32((uint32_t)sc[0] | ((uint32_t)sc[2] << 8), s0, s1);
+                    e4m3x2_to_f32((uint32_t)lo[0] | ((uint32_t)lo[2] << 8), l0, l1);
+                    const float pw = (p == 0) ? pws[0] : (p == 2) ? pws[2] : pws[1];
+                    cst[2 * idx] = pack_bf16(s0 * pw, s1 * pw);
+                    cst[2 * idx + 1] = pack_bf16(l0, l1);
+                }
 #pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const int t = tid + 128 * e;
-                float vl0, vl1, vs0, vs1;
-                e4m3x2_to_f32(*reinterpret_cast<const uint16_t*>(raw + VLO_O + 2 * t), vl0, vl1);
-                e4m3x2_to_f32(*reinterpret_cast<const uint16_t*>(raw + VSC_O + 2 * t), vs0, vs1);
-                vsl[2 * t] = make_float2(vl0, vs0);
-                vsl[2 * t + 1] = make_float2(vl1, vs1);
+                for (int e = 0; e < 2; e++) {
+                    const int t = tid + 128 * e;
+                    float vl0, vl1, vs0, vs1;
+                    e4m3x2_to_f32(*reinterpret_cast<const uint16_t*>(raw + ST_SC + 2 * t), vl0, vl1);
+                    e4m3x2_to_f32(*reinterpret_cast<const uint16_t*>(raw + ST_SC + (VSC_O - VLO_O) + 2 * t), vs0,
+                                  vs1);
+                    vsl[2 * t] = make_float2(vl0, vs0);
+                    vsl[2 * t + 1] = make_float2(vl1, vs1);
+                }
             }
+            __syncthreads();
         }
-        __syncthreads();
         if (ok) {
             DequantConsts K;
             {
@@ -445,9 +476,18 @@ __global__ void __launch_bounds__(128, 2) qdecode_mma(QMArgs a) {
                     K.A[p][2] = w1.x; K.L[p][2] = w1.y; K.A[p][3] = w1.z; K.L[p][3] = w1.w;
                 }
             }
-            const int64_t pos0 = jb * BLK;
+            const int64_t pos0 = jb * BLK + half * QM_HALF;   // position of the half's first token
+            const float2* vslh = vsl + 2 * half * QM_HALF;
+            // cos / sin rows of the tile's tokens t0 + g and t0 + g + 8 (this thread's 8 frequencies): loaded one
+            // 16-token tile ahead so the L2 latency of the table overlaps the previous tile's work
+            const uint16_t* crow0 = a.cos_t + (pos0 + g) * 32 + 8 * tig;
+            const uint16_t* srow0 = a.sin_t + (pos0 + g) * 32 + 8 * tig;
+            uint4 pf_ca = *reinterpret_cast<const uint4*>(crow0);
+            uint4 pf_sa = *reinterpret_cast<const uint4*>(srow0);
+            uint4 pf_cb = *reinterpret_cast<const uint4*>(crow0 + 8 * 32);
+            uint4 pf_sb = *reinterpret_cast<const uint4*>(srow0 + 8 * 32);
 #pragma unroll 1
-            for (int c0 = 0; c0 < BLK; c0 += 32) {
+            for (int c0 = 0; c0 < QM_HALF; c0 += 32) {
                 float sc[2][4];
                 float vsv[2][2], vlv[2][2];
 #pragma unroll
@@ -458,21 +498,29 @@ __global__ void __launch_bounds__(128, 2) qdecode_mma(QMArgs a) {
                         const uint8_t* kt = raw + t0 * 128;
                         const uint2 kwa = *reinterpret_cast<const uint2*>(kt + koff_a);
                         const uint2 kwb = *reinterpret_cast<const uint2*>(kt + koff_b);
-                        const uint16_t* crow = a.cos_t + (pos0 + t0 + g) * 32 + 8 * tig;
-                        const uint16_t* srow = a.sin_t + (pos0 + t0 + g) * 32 + 8 * tig;
-                        const uint4 ca = *reinterpret_cast<const uint4*>(crow);
-                        const uint4 sa = *reinterpret_cast<const uint4*>(srow);
-                        const uint4 cb = *reinterpret_cast<const uint4*>(crow + 8 * 32);
-                        const uint4 sbw = *reinterpret_cast<const uint4*>(srow + 8 * 32);
+                        const uint4 ca = pf_ca, sa = pf_sa, cb = pf_cb, sbw = pf_sb;
+                        if (t0 + 16 < QM_HALF) {
+                            const uint16_t* crow = crow0 + (t0 + 16) * 32;
+                            const uint16_t* srow = srow0 + (t0 + 16) * 32;
+                            pf_ca = *reinterpret_cast<const uint4*>(crow);
+                            pf_sa = *reinterpret_cast<const uint4*>(srow);
+                            pf_cb = *reinterpret_cast<const uint4*>(crow + 8 * 32);
+                            pf_sb = *reinterpret_cast<const uint4*>(srow + 8 * 32);
+                        }
                         token_regs(kwa.x, kwa.y, ca, sa, K, R0);
                         token_regs(kwb.x, kwb.y, cb, sbw, K, R1);
                     }
+                    // two accumulator chains (even / odd K-steps) halve the dependent-MMA latency
+                    float sx[4] = {0.f, 0.f, 0.f, 0.f}, sy[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                    for (int e = 0; e < 4; e++) sc[mt][e] = 0.f;
+                    for (int ks = 0; ks < 8; ks += 2) {
+                        mma_bf16(sx, R0[2 * ks], R1[2 * ks], R0[2 * ks + 1], R1[2 * ks + 1], bq[ks][0], bq[ks][1]);
+                        mma_bf16(sy, R0[2 * ks + 2], R1[2 * ks + 2], R0[2 * ks + 3], R1[2 * ks + 3], bq[ks + 1][0],
+                                 bq[ks + 1][1]);
+                    }
 #pragma unroll
-                    for (int ks = 0; ks < 8; ks++)
-                        mma_bf16(sc[mt], R0[2 * ks], R1[2 * ks], R0[2 * ks + 1], R1[2 * ks + 1], bq[ks][0], bq[ks][1]);
-                    const float2 xa = vsl[2 * t0 + vsl_a], xb = vsl[2 * t0 + vsl_b];
+                    for (int e = 0; e < 4; e++) sc[mt][e] = sx[e] + sy[e];
+                    const float2 xa = vslh[2 * t0 + vsl_a], xb = vslh[2 * t0 + vsl_b];
                     vlv[mt][0] = xa.x; vsv[mt][0] = xa.y;
                     vlv[mt][1] = xb.x; vsv[mt][1] = xb.y;
                 }
@@ -488,7 +536,7 @@ __global__ void __launch_bounds__(128, 2) qdecode_mma(QMArgs a) {
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
                     if (mx > m[rr] + 6.0f) {
-                        alpha[rr] = exp2f(m[rr] - mx);
+                        alpha[rr] = fast_exp2(m[rr] - mx);
                         m[rr] = mx;
                         moved = true;
                     }
@@ -497,7 +545,7 @@ __global__ void __launch_bounds__(128, 2) qdecode_mma(QMArgs a) {
 #pragma unroll
                 for (int mt = 0; mt < 2; mt++)
 #pragma unroll
-                    for (int e = 0; e < 4; e++) p[mt][e] = exp2f(fmaf(sc[mt][e], a.scale, -m[e & 1]));
+                    for (int e = 0; e < 4; e++) p[mt][e] = fast_exp2(fmaf(sc[mt][e], a.scale, -m[e & 1]));
                 if (__any_sync(0xffffffffu, moved)) {
 #pragma unroll
                     for (int rr = 0; rr < 2; rr++) {
@@ -547,11 +595,12 @@ __global__ void __launch_bounds__(128, 2) qdecode_mma(QMArgs a) {
                 }
             }
         }
-        __syncthreads();   // stage (i & 1) and cst / vsl free again
-        if (i + 2 < n) {
+        __syncthreads();   // stage (k & 1) free again (and cst / vsl once the second half is done)
+        if (k + 2 < 2 * n) {
+            const int i2 = (k + 2) >> 1;
             const uint8_t* src2;
-            if (persistent) advance(pre, u0 + i + 2);
-            if (sub_ok(a, pre.b, u0 + i + 2 - pre.rs, src2)) stage_subblock(raw, src2, tid);
+            if (persistent) advance(pre, u0 + i2);
+            if (sub_ok(a, pre.b, u0 + i2 - pre.rs, src2)) stage_half(raw, src2, (k + 2) & 1, tid);
         }
         cp_commit();
     }

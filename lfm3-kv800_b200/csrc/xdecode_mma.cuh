@@ -234,14 +234,14 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
             if (mx > m[rr] + 6.0f) {
-                alpha[rr] = exp2f(m[rr] - mx);
+                alpha[rr] = fast_exp2(m[rr] - mx);
                 m[rr] = mx;
                 moved = true;
             }
         }
         float p[4];
 #pragma unroll
-        for (int k = 0; k < 4; k++) p[k] = exp2f(s2[k] - m[k & 1]);
+        for (int k = 0; k < 4; k++) p[k] = fast_exp2(s2[k] - m[k & 1]);
         if (__any_sync(0xffffffffu, moved)) {
             l_part[0] *= alpha[0];
             l_part[1] *= alpha[1];

@@ -62,7 +62,7 @@ def test_host_argument_checks():
     assert L.kv800_check_status(None, None, None) == _lib.ERR_ARG
 
 
-def _plan_bytes(B, nqmax, win, spb, G0=296):
+def _plan_bytes(B, nqmax, win, spb, G0=444):
     up = lambda x: (x + 255) & ~255
     nq = 0 if win else nqmax
     persistent = spb <= 0 and nq > 0
