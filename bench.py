@@ -204,6 +204,61 @@ def cpu_sample(layers, qs, c32, s32, S, reps=1):
     return S / best, best
 
 
+# ---------------------------------------------------------------- flush / quantize (config 2)
+def flush_bench(kv800, torch, dev, reps=10):
+    """Config 2 of BASELINE: K / V ~ N(0, 1) bf16 with 1 % of the channels x 8.  (a) prefill: 16 sequences x 2048
+    tokens = 112 full sub-blocks quantized in one quantize_blocks call; (b) decode step: 256 sequences whose new token
+    completes a flush boundary, one 256-token sub-block each gathered from shuffled exact pages by the paged flush.
+    Reports sub-blocks/s and the bytes moved (524,288 read + 51,200 written per sub-block)."""
+    g = torch.Generator(device="cpu").manual_seed(7)
+    def kvgen(M):
+        k = torch.randn(M, 256, 4, 128, generator=g)
+        v = torch.randn(M, 256, 4, 128, generator=g)
+        mk = torch.rand(4, 128, generator=g) < 0.01
+        mv = torch.rand(4, 128, generator=g) < 0.01
+        k = torch.where(mk, k * 8, k).to(torch.bfloat16).to(dev)
+        v = torch.where(mv, v * 8, v).to(torch.bfloat16).to(dev)
+        return k, v
+    k, v = kvgen(112)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / reps
+
+    t_pre = timed(lambda: kv800.quantize_blocks(k, v))
+    # 256 sequences: exact pages of 64 tokens at shuffled slots, sub-block 0 of each (positions 0..255) flushed
+    B, ebs = 256, 64
+    kk, vv = kvgen(B)
+    perm = torch.randperm(B * 4 + 5, generator=g)[:B * 4].view(B, 4)
+    eoff = (perm * (4 * ebs * 256)).to(torch.int64).to(dev)
+    epool = torch.zeros(B * 4 + 5, 4, ebs, 256, dtype=torch.bfloat16, device=dev)
+    seq = torch.arange(B, dtype=torch.int32, device=dev).repeat_interleave(256)
+    pos = torch.arange(256, dtype=torch.int64, device=dev).repeat(B)
+    kv800.write_exact(epool, eoff, ebs, ebs * 256, 256, 128, kk.reshape(-1, 4, 128), vv.reshape(-1, 4, 128), seq,
+                      pos)
+    qpool = torch.zeros(B + 3, 51200, dtype=torch.uint8, device=dev)
+    boff = (torch.randperm(B + 3, generator=g)[:B] * 51200).to(torch.int64).view(B, 1).to(dev)
+    sidx = torch.arange(B, dtype=torch.int32, device=dev)
+    zero = torch.zeros(B, dtype=torch.int32, device=dev)
+    t_step = timed(lambda: kv800.flush(epool, eoff, ebs, ebs * 256, 256, 128, qpool, boff, sidx, zero))
+    per = 524288 + 51200
+    return {"prefill_subblocks": 112, "prefill_us": round(t_pre * 1e6, 1),
+            "prefill_subblocks_per_s": round(112 / t_pre, 1), "prefill_tok_per_s": round(112 * 256 / t_pre, 1),
+            "prefill_gbs": round(112 * per / t_pre / 1e9, 1),
+            "step_flush_subblocks": B, "step_flush_us": round(t_step * 1e6, 1),
+            "step_flush_gbs": round(B * per / t_step / 1e9, 1),
+            "bound": "fp32 FMA (16.8 M FMA per sub-block for the bit-exact Hadamard chain)",
+            "fma_tflops": round(2 * 16.8e6 * 112 / t_pre / 1e12, 1)}
+
+
 # ---------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -214,6 +269,7 @@ def main():
     ap.add_argument("--cpu-seqs", type=int, default=8, help="sequences of the CPU-baseline sample")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-flush", action="store_true", help="skip the quantize / flush measurement")
     ap.add_argument("--seqs", type=int, default=B_PER_GPU, help="sequences per GPU (profiling: smaller cases)")
     ap.add_argument("--ctx", type=int, default=N_CTX, help="context length (profiling: smaller cases)")
     a = ap.parse_args()
@@ -333,6 +389,12 @@ def main():
         e2e = {"value": round(a.seqs * a.steps * n_gpus / te, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": round(te / a.steps * 1e3, 4)}
 
+    # ---- flush / quantize: a 16 x 2048-token prefill (112 sub-blocks through quantize_blocks)
+    # and a decode step of 256 sequences that crosses a flush boundary (one sub-block each through the paged flush)
+    flush = None
+    if not a.no_flush:
+        flush = flush_bench(kv800, torch, dev)
+
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu:
         S = a.cpu_seqs
@@ -355,7 +417,7 @@ def main():
                 "hbm_gbs_step": round(step_bytes * a.steps / t / 1e9, 1),
                 "hbm_frac_step": round(step_bytes * a.steps / t / 1e9 / peaks()[0], 4),
                 "bytes_per_step_per_gpu": step_bytes, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_launches": launches_per_step * a.steps, "clocks": clocks}
+                "gpu_launches": launches_per_step * a.steps, "clocks": clocks, "flush": flush}
         print(json.dumps(line), flush=True)
 
 

@@ -62,6 +62,17 @@ KV800_API int kv800_quantize_blocks(const uint16_t* k, const uint16_t* v, int64_
 KV800_API int kv800_dequantize_blocks(const uint8_t* sb, int64_t M, uint16_t* k_out, float* v_out, void* stream);
 
 /*
+ * kv800_fake_quant_k / kv800_fake_quant_v -- replace train.fake_quant_k(x) and train.fake_quant_v(v, H)
+ * (lfm3_kv800/train.py:82-100): the cache's quantize -> dequantize round trip on fp32 training activations.
+ * fake_quant_k: x (G, 256, C) fp32 (256-token groups on dim 1) -> out (G, 256, C) fp32 = code * sc8 + lo8 per
+ * (group, channel).  fake_quant_v: v (N, 4, 128) fp32 -> out (N, 4, 128) fp32 = ((v @ H) quantized to 1 bit per dim
+ * over 2-head groups, dequantized) @ H, with the same sequential FMA chain as the quantizer (bit-exact with the
+ * reference on CPU).
+ */
+KV800_API int kv800_fake_quant_k(const float* x, int64_t G, int64_t C, float* out, void* stream);
+KV800_API int kv800_fake_quant_v(const float* v, int64_t N, float* out, void* stream);
+
+/*
  * kv800_flush -- replaces the flush of PagedStore.append (kv800.py:433-440) and of the vLLM backend
  * (vllm_attn.py:298-317): for m < M, gather the 256 exact tokens of sub-block blk[m] of sequence seq[m] (positions
  * [256 blk, 256 blk + 256)) from the exact pages, quantize them as kv800_quantize_blocks does, and write the 51,200

@@ -320,6 +320,81 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* sb_all, uin
     }
 }
 
+// ---- training-side fake quantization (lfm3_kv800/train.py:82-100): the cache's quantize -> dequantize round trip
+// on fp32 activations without packing.
+// K: x (G, 256, C) fp32, groups of 256 tokens per channel: lo / hi, fp8 lo and (hi - lo) / 3 scale, code =
+// round((x - lo8) / sc8) in [0, 3], out = code * sc8 + lo8.  grid (G, ceil(C / 128)), thread = channel.
+__global__ void __launch_bounds__(128) fake_quant_k_kernel(const float* x, int64_t C, float* out) {
+    const int64_t g = blockIdx.x, c = (int64_t)blockIdx.y * 128 + threadIdx.x;
+    if (c >= C) return;
+    const float* col = x + g * BLK * C + c;
+    float lo = __int_as_float(0x7f800000), hi = -__int_as_float(0x7f800000);
+    for (int t = 0; t < BLK; t++) {
+        const float v = col[(int64_t)t * C];
+        lo = fminf(lo, v);
+        hi = fmaxf(hi, v);
+    }
+    const float lof = f8dec(f8enc(lo));
+    const float scq = f8dec(f8enc(clamp_min_1e8(__fdiv_rn(hi - lo, 3.0f))));
+    const float scf = clamp_min_1e8(scq);
+    float* oc = out + g * BLK * C + c;
+    for (int t = 0; t < BLK; t++) {
+        const float v = col[(int64_t)t * C];
+        const float code = (float)round_clamp(__fdiv_rn(v - lof, scf), 3.0f);
+        oc[(int64_t)t * C] = fmaf(code, scq, lof);   // code * sc8 is exact, so this is the reference's mul + add
+    }
+}
+
+// V: v (N, 4, 128) fp32 per token: y = v @ H per head (sequential FMA chain), per 2-head group lo / hi, fp8 lo and
+// scale hi - lo, bit = round((y - lo8) / sc8) in [0, 1], out = (bit * sc8 + lo8) @ H.  Warp per token.
+__global__ void __launch_bounds__(256) fake_quant_v_kernel(const float* v, int64_t N, float* out) {
+    __shared__ float buf[8][HEADS * DIM];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t t = (int64_t)blockIdx.x * 8 + warp;
+    if (t >= N) return;
+    float C[32];
+    hadamard_signs(lane, C);
+    const float* row = v + t * HEADS * DIM;
+#pragma unroll
+    for (int i = 0; i < 16; i++) buf[warp][lane + 32 * i] = row[lane + 32 * i];
+    __syncwarp();
+    float y[HEADS][4];
+    hadamard_rows(buf[warp], C, y);
+    __syncwarp();
+#pragma unroll
+    for (int g2 = 0; g2 < 2; g2++) {
+        float l = y[2 * g2][0], u = y[2 * g2][0];
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                l = fminf(l, y[2 * g2 + hh][k]);
+                u = fmaxf(u, y[2 * g2 + hh][k]);
+            }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            l = fminf(l, __shfl_xor_sync(0xffffffffu, l, o));
+            u = fmaxf(u, __shfl_xor_sync(0xffffffffu, u, o));
+        }
+        const float lof = f8dec(f8enc(l)), scq = f8dec(f8enc(clamp_min_1e8(u - l)));
+        const float scf = clamp_min_1e8(scq);
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float bit = (float)round_clamp(__fdiv_rn(y[2 * g2 + hh][k] - lof, scf), 1.0f);
+                buf[warp][(2 * g2 + hh) * DIM + lane + 32 * k] = fmaf(bit, scq, lof);
+            }
+    }
+    __syncwarp();
+    hadamard_rows(buf[warp], C, y);
+    float* orow = out + t * HEADS * DIM;
+#pragma unroll
+    for (int h = 0; h < HEADS; h++)
+#pragma unroll
+        for (int k = 0; k < 4; k++) orow[h * DIM + lane + 32 * k] = y[h][k];
+}
+
 // Exact-page scatter: one warp per (token, head, K|V) row of 128 bf16 (256 B, 8 B per lane).
 __global__ void write_exact_kernel(uint16_t* epool, int64_t epool_elems, const int64_t* eoff, int64_t eoff_stride,
                                    int64_t ebs, int64_t e_hs, int64_t e_ts, int64_t e_v, const uint16_t* k,
@@ -425,4 +500,33 @@ extern "C" int kv800_dequantize_blocks(const uint8_t* sb, int64_t M, uint16_t* k
     }
     dequant_kernel<<<dim3((unsigned)M, 8), 256, 0, as_stream(stream)>>>(sb, k_out, v_out);
     return cuda_status(cudaGetLastError(), "kv800_dequantize_blocks launch");
+}
+
+extern "C" int kv800_fake_quant_k(const float* x, int64_t G, int64_t C, float* out, void* stream) {
+    if (G < 0 || C < 0 || ((G > 0 && C > 0) && (!x || !out))) {
+        set_error("kv800_fake_quant_k: null pointer or negative size");
+        return KV800_ERR_ARG;
+    }
+    if (G == 0 || C == 0) return KV800_OK;
+    if (G > 0x7fffffffLL || (C + 127) / 128 > 65535) {
+        set_error("kv800_fake_quant_k: G %lld / C %lld above the grid limits", (long long)G, (long long)C);
+        return KV800_ERR_RANGE;
+    }
+    fake_quant_k_kernel<<<dim3((unsigned)G, (unsigned)((C + 127) / 128)), 128, 0, as_stream(stream)>>>(x, C, out);
+    return cuda_status(cudaGetLastError(), "kv800_fake_quant_k launch");
+}
+
+extern "C" int kv800_fake_quant_v(const float* v, int64_t N, float* out, void* stream) {
+    if (N < 0 || (N > 0 && (!v || !out))) {
+        set_error("kv800_fake_quant_v: null pointer or negative N");
+        return KV800_ERR_ARG;
+    }
+    if (N == 0) return KV800_OK;
+    const int64_t blocks = (N + 7) / 8;
+    if (blocks > 0x7fffffffLL) {
+        set_error("kv800_fake_quant_v: N %lld too large", (long long)N);
+        return KV800_ERR_RANGE;
+    }
+    fake_quant_v_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(v, N, out);
+    return cuda_status(cudaGetLastError(), "kv800_fake_quant_v launch");
 }

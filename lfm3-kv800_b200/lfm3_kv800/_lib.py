@@ -27,6 +27,8 @@ SIGNATURES = {
     "kv800_constants": (_int, [_p, _p, _p, _p, _p]),
     "kv800_quantize_blocks": (_int, [_p, _p, _i64, _p, _p]),
     "kv800_dequantize_blocks": (_int, [_p, _i64, _p, _p, _p]),
+    "kv800_fake_quant_k": (_int, [_p, _i64, _i64, _p, _p]),
+    "kv800_fake_quant_v": (_int, [_p, _i64, _p, _p]),
     "kv800_flush": (_int, [_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _i64, _p, _p, _i64, _i64, _p,
                            _p]),
     "kv800_write_exact": (_int, [_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p]),

@@ -365,6 +365,70 @@ void orc_decode(const uint8_t* qpool, const int64_t* boff, int64_t boff_stride, 
     }
 }
 
+/* ------------------------------------------------------------------ training fake quant (train.py:82-100) */
+/* fake_quant_k: x (G, 256, C) fp32 -> out: per (group, channel) lo / hi over the 256 tokens, lo8 = fp8(lo),
+ * sc8 = fp8(max((hi - lo) / 3, 1e-8)), code = clamp(round((x - lo8) / max(sc8, 1e-8)), 0, 3), out = code * sc8 + lo8. */
+void orc_fake_quant_k(const float* x, int64_t G, int64_t C, float* out, int nthreads) {
+#pragma omp parallel for num_threads(nthreads > 0 ? nthreads : 1) schedule(static)
+    for (int64_t gc = 0; gc < G * C; gc++) {
+        int64_t g = gc / C, c = gc % C;
+        const float* col = x + g * BLK * C + c;
+        float lo = INFINITY, hi = -INFINITY;
+        for (int t = 0; t < BLK; t++) {
+            float v = col[(int64_t)t * C];
+            lo = v < lo ? v : lo;
+            hi = v > hi ? v : hi;
+        }
+        float lof = orc_f8_decode(orc_f8_encode(lo));
+        float scq = orc_f8_decode(orc_f8_encode(clamp_min_1e8((hi - lo) / 3.0f)));
+        float scf = clamp_min_1e8(scq);
+        for (int t = 0; t < BLK; t++) {
+            float v = col[(int64_t)t * C];
+            float code = (float)round_clamp_u8((v - lof) / scf, 3.0f);
+            float prod = code * scq;
+            out[g * BLK * C + (int64_t)t * C + c] = prod + lof;
+        }
+    }
+}
+
+/* fake_quant_v: v (N, 4, 128) fp32 -> ((v @ H) 1-bit quantized over 2-head groups of 256 dims, fp8 lo and scale
+ * hi - lo, dequantized) @ H; both products as the sequential fp32 FMA chain. */
+void orc_fake_quant_v(const float* v, int64_t N, float* out, int nthreads) {
+#pragma omp parallel for num_threads(nthreads > 0 ? nthreads : 1) schedule(static)
+    for (int64_t t = 0; t < N; t++) {
+        const float* row = v + t * 512;
+        float y[512], yq[512];
+        for (int h = 0; h < 4; h++)
+            for (int d = 0; d < 128; d++) {
+                float acc = 0.0f;
+                for (int i = 0; i < 128; i++) acc = fmaf(row[h * 128 + i], had(i, d), acc);
+                y[h * 128 + d] = acc;
+            }
+        for (int g = 0; g < 2; g++) {
+            float lo = INFINITY, hi = -INFINITY;
+            for (int e = 0; e < 256; e++) {
+                float x = y[g * 256 + e];
+                lo = x < lo ? x : lo;
+                hi = x > hi ? x : hi;
+            }
+            float lof = orc_f8_decode(orc_f8_encode(lo));
+            float scq = orc_f8_decode(orc_f8_encode(clamp_min_1e8(hi - lo)));
+            float scf = clamp_min_1e8(scq);
+            for (int e = 0; e < 256; e++) {
+                float bit = (float)round_clamp_u8((y[g * 256 + e] - lof) / scf, 1.0f);
+                float prod = bit * scq;
+                yq[g * 256 + e] = prod + lof;
+            }
+        }
+        for (int h = 0; h < 4; h++)
+            for (int d = 0; d < 128; d++) {
+                float acc = 0.0f;
+                for (int i = 0; i < 128; i++) acc = fmaf(yq[h * 128 + i], had(i, d), acc);
+                out[t * 512 + h * 128 + d] = acc;
+            }
+    }
+}
+
 /* fp32 -> fp8 over an array (checks the encoder against torch on CPU). */
 void orc_f8_encode_array(const float* x, int64_t n, uint8_t* out) {
     for (int64_t i = 0; i < n; i++) out[i] = orc_f8_encode(x[i]);

@@ -9,6 +9,7 @@ Reference anchors (riceharvest/lfm3-kv800 v0.1.1):
   dequantize_blocks    lfm3_kv800/kv800.py:79-92
   decode               lfm3_kv800/torch_decode.py:27-80
   Store                lfm3_kv800/kv800.py:387-441 (PagedStore: exact ring pages, flush rule n >= 256 j + 384)
+  fake_quant_k / _v    lfm3_kv800/train.py:82-100
 Parity of this oracle with the reference is pinned by the fixtures in tests/golden (made by make_golden.py, which
 imports the reference)."""
 import ctypes
@@ -51,6 +52,8 @@ def lib():
         L.orc_decode.argtypes = [_p, _p, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _i64,
                                  _i64, _p, _p, _p, _i64, _p, _int]
         L.orc_f8_encode_array.argtypes = [_p, _i64, _p]
+        L.orc_fake_quant_k.argtypes = [_p, _i64, _i64, _p, _int]
+        L.orc_fake_quant_v.argtypes = [_p, _i64, _p, _int]
         _lib = L
     return _lib
 
@@ -112,6 +115,26 @@ def dequantize_blocks(sb):
     v = np.empty((M, BLK, 4, 128), np.float32)
     lib().orc_dequantize_blocks(_ptr(sb), M, _ptr(k), _ptr(v), None)
     return k, v
+
+
+# ---------------------------------------------------------------- training fake quant (train.py:82-100)
+def fake_quant_k(x, nthreads=None):
+    """x (..., G, 256, C) float32 -> the 800h K quantize-dequantize round trip (float32), per 256-token group and
+    channel."""
+    x = _c(x, np.float32)
+    C = x.shape[-1]
+    G = x.size // (BLK * C)
+    out = np.empty_like(x)
+    lib().orc_fake_quant_k(_ptr(x), G, C, _ptr(out), nthreads or threads())
+    return out
+
+
+def fake_quant_v(v, nthreads=None):
+    """v (..., 4, 128) float32 -> the 800h V round trip through the Hadamard domain (float32)."""
+    v = _c(v, np.float32)
+    out = np.empty_like(v)
+    lib().orc_fake_quant_v(_ptr(v), v.size // 512, _ptr(out), nthreads or threads())
+    return out
 
 
 # ---------------------------------------------------------------- paged decode

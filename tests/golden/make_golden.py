@@ -11,7 +11,9 @@ fixtures it writes are committed and are all the tests need elsewhere.  What is 
   decode.npz  the 12 cases of the reference parity test (tests/test_parity.py:17-18,80-96) driven through
               kv800.PagedStore.append (flush rule, kv800.py:421-441) and torch_decode.decode (torch_decode.py:27-80):
               the bf16 outputs, the sha256 of the quantized pool and the exact pool after the appends, and the error
-              of the reference's own torch backend against the test's dense re-derivation"""
+              of the reference's own torch backend against the test's dense re-derivation
+  fakequant.npz  train.fake_quant_k / fake_quant_v (train.py:82-100) on three input kinds: sha256 of the fp32
+              outputs, the first 16 tokens raw for the 'outlier' kind"""
 import argparse
 import os
 import sys
@@ -86,6 +88,23 @@ def main():
         d[f"{key}_rel_vs_dense"] = np.float64(rel)
         print(f"decode win={win} n={n}: nq={st.nq} rel(torch_decode vs dense)={rel:.3e}", flush=True)
     np.savez_compressed(os.path.join(HERE, "decode.npz"), **d)
+
+    # ------------------------------------------------------------ training fake quant (train.py:82-100)
+    from lfm3_kv800 import train as kt
+    f = {}
+    for kind in ("normal", "outlier", "edge"):
+        k, v = I.quant_inputs(kind, 2, seed=3)
+        kf = I.bf16_to_f32(k).reshape(2, 256, 512)        # groups of 256 tokens x 512 channels, as fq_k feeds it
+        vf = I.bf16_to_f32(v)
+        fk = kt.fake_quant_k(torch.from_numpy(kf.copy())).numpy()
+        fv = kt.fake_quant_v(torch.from_numpy(vf.copy()), kt.hadamard(128)).numpy()
+        f[f"{kind}_k_sha"] = np.array(I.digest(fk))
+        f[f"{kind}_v_sha"] = np.array(I.digest(fv))
+        if kind == "outlier":                             # a slice of raw values for readable diffs
+            f["outlier_k16"] = fk[0, :16]
+            f["outlier_v16"] = fv[0, :16]
+        print(f"fake quant {kind} ok", flush=True)
+    np.savez_compressed(os.path.join(HERE, "fakequant.npz"), **f)
 
 
 if __name__ == "__main__":

@@ -84,3 +84,29 @@ def test_flush_rule(i):
     z = np.zeros((1, n, 4, 128), np.uint16)
     st.append(z, z)
     assert st.nq == max(0, n - 128) // 256
+
+
+FG = np.load(I.__file__.replace("inputs.py", "fakequant.npz"))
+
+
+@pytest.mark.parametrize("kind", ["normal", "outlier", "edge"])
+def test_fake_quant_matches_reference(kind):
+    """The training-side fake quant (train.py:82-100): K bit-exact, V bit-exact (same FMA chain as the CPU BLAS)."""
+    k, v = I.quant_inputs(kind, 2, seed=3)
+    fk = O.fake_quant_k(I.bf16_to_f32(k).reshape(2, 256, 512))
+    fv = O.fake_quant_v(I.bf16_to_f32(v))
+    if kind == "outlier":
+        np.testing.assert_array_equal(fk[0, :16], FG["outlier_k16"])
+        np.testing.assert_array_equal(fv[0, :16], FG["outlier_v16"])
+    assert I.digest(fk) == str(FG[f"{kind}_k_sha"])
+    assert I.digest(fv) == str(FG[f"{kind}_v_sha"])
+
+
+def test_fake_quant_k_equals_cache_round_trip():
+    """Reference tests/test_train_hook.py:92-106: the K fake quant equals dequantize(quantize(.)) of the cache."""
+    k, v = I.quant_inputs("outlier", 3, seed=8)
+    kd, vd = O.dequantize_blocks(O.quantize_blocks(k, v))
+    fk = O.fake_quant_k(I.bf16_to_f32(k).reshape(3, 256, 512)).reshape(3, 256, 4, 128)
+    np.testing.assert_array_equal(I.f32_to_bf16(fk), kd)
+    fv = O.fake_quant_v(I.bf16_to_f32(v))
+    np.testing.assert_allclose(fv, vd, atol=1e-5, rtol=0)
