@@ -87,6 +87,81 @@ KV800_API int kv800_flush(const uint16_t* epool, int64_t epool_elems, const int6
                 void* stream);
 
 /*
+ * kv800_flush_step -- the flush of one vLLM step (vllm_attn.py:298-317) without a host loop.  The flush plan is built
+ * on the device: request b (seq_lens[b] tokens after the step, query_start_loc[b + 1] - query_start_loc[b] of them new)
+ * owns sub-blocks j in [nq(prev), nq(seq_lens[b])), nq(n) = max(0, n - 128) / 256, listed in request order (at most
+ * max_pairs; more sets ST_TABLE in *status).  Each listed sub-block is gathered from the exact cache, quantized and
+ * written to the quant cache in the same stream.  Replaces the reference's Python plan loop and per-element
+ * index tensors (vllm_attn.py:300-317).
+ *   exact cache  [blocks, 4, ebs, 256] bf16 with element strides s0 (block), s1 (head), s2 (row); K of (block, head,
+ *                row) at blk * s0 + h * s1 + row * s2, V at + 128.  block_table: int32, row stride bt_stride, maps
+ *                (request, position / ebs) to a block.
+ *   quant cache  pages of qs0 bytes holding bsq / 256 sub-blocks of 51,200 B; qblock_table maps (request, 256 j / bsq)
+ *                to a page.
+ *   seq_lens, query_start_loc  int32 device arrays (R and R + 1 entries), as vLLM's attention metadata holds them.
+ *   workspace    kv800_flush_step_workspace_size(max_pairs) bytes, 256-aligned (holds the plan).
+ */
+KV800_API int64_t kv800_flush_step_workspace_size(int64_t max_pairs);
+KV800_API int kv800_flush_step(const uint16_t* ecache, int64_t ecache_elems, int64_t s0, int64_t s1, int64_t s2,
+                               int64_t ebs, const int32_t* block_table, int64_t bt_stride, uint8_t* qcache,
+                               int64_t qcache_bytes, int64_t qs0, int64_t bsq, const int32_t* qblock_table,
+                               int64_t qbt_stride, const int32_t* seq_lens, const int32_t* query_start_loc, int64_t R,
+                               int64_t max_pairs, void* workspace, int64_t workspace_bytes, int* status,
+                               void* stream);
+
+/*
+ * kv800_write_sinks -- the sink write of a window layer (vllm_attn.py:276-291): token i with positions[i] < 4 (and
+ * slot_mapping[i] >= 0) of request b (query_start_loc[b] <= i < query_start_loc[b + 1]) writes its K rows to
+ * hk + hk_bt[b * hk_bts] * hk_s0 + hk_aux + (p * 4 + h) * 128 and its V rows likewise into hv (bf16 views of the two
+ * host layers' quant caches; aux = the element offset of the page padding).  Out-of-range rows set ST_SINK.
+ */
+KV800_API int kv800_write_sinks(uint16_t* hk, int64_t hk_elems, int64_t hk_s0, int64_t hk_aux, const int32_t* hk_bt,
+                                int64_t hk_bts, uint16_t* hv, int64_t hv_elems, int64_t hv_s0, int64_t hv_aux,
+                                const int32_t* hv_bt, int64_t hv_bts, const uint16_t* k, const uint16_t* v,
+                                const int64_t* positions, const int64_t* slot_mapping, const int32_t* query_start_loc,
+                                int64_t R, int64_t T, int* status, void* stream);
+
+/*
+ * kv800_decode_tables -- the decode inputs of the first nd requests of a vLLM step (vllm_attn.py:320-349) in one
+ * launch: N = seq_lens, NQ = max(0, N - 128) / 256 (0 when qblock_table is null), eoff[b, c] = block_table[b, c] * s0
+ * ([nd, bt_stride] int64), boff[b, j] = qblock_table[b, 256 j / bsq] * qs0 + ((256 j % bsq) / 256) * 51200 for
+ * j < NQ[b] and 0 beyond ([nd, nqw] int64), and for window layers skoff / svoff = host_bt[b, 0] * s0 + aux (pass null
+ * to skip).
+ */
+KV800_API int kv800_decode_tables(const int32_t* seq_lens, int64_t nd, const int32_t* block_table, int64_t bt_stride,
+                                  int64_t s0, int32_t* N, int32_t* NQ, int64_t* eoff, const int32_t* qblock_table,
+                                  int64_t qbt_stride, int64_t qs0, int64_t bsq, int64_t nqw, int64_t* boff,
+                                  const int32_t* sk_bt, int64_t sk_bts, int64_t sk_s0, int64_t sk_aux, int64_t* skoff,
+                                  const int32_t* sv_bt, int64_t sv_bts, int64_t sv_s0, int64_t sv_aux, int64_t* svoff,
+                                  void* stream);
+
+/*
+ * kv800_prefill_kv -- the K / V a prefill or extend request attends to, in position order (vllm_attn.py:355-388):
+ * sub-blocks j < nqp dequantized from the quant cache (qbt_row: the request's quant block-table row), ns <= 4 sink
+ * rows (sk / sv: (ns, 4, 128) bf16), exact rows of positions [lo, n0) from the exact cache (bt_row), and the chunk k / v
+ * ((n - n0, 4, 128) bf16, positions n0 .. n - 1).  K is rotated with the [npos, 32] bf16 cos / sin tables (HF RoPE in
+ * the reference's fp32 operation order, then bf16) unless cos_t and sin_t are null (native sliding layers); V is bf16.
+ * k_out / v_out: (256 nqp + ns + (n0 - lo) + (n - n0), 4, 128) bf16.  Bit-identical to the reference's
+ * dequantize_blocks + cat + _rope + bf16 casts.
+ */
+KV800_API int kv800_prefill_kv(const uint8_t* qcache, int64_t qcache_bytes, int64_t qs0, int64_t bsq,
+                               const int32_t* qbt_row, int64_t qbt_len, int64_t nqp, const uint16_t* sk,
+                               const uint16_t* sv, int64_t ns, const uint16_t* ecache, int64_t ecache_elems, int64_t s0,
+                               int64_t s1, int64_t s2, int64_t ebs, const int32_t* bt_row, int64_t bt_len, int64_t lo,
+                               int64_t n0, const uint16_t* k, const uint16_t* v, int64_t n, const uint16_t* cos_t,
+                               const uint16_t* sin_t, int64_t npos, uint16_t* k_out, uint16_t* v_out, int* status,
+                               void* stream);
+
+/*
+ * kv800_write_slots -- the exact-cache write of a vLLM step (vllm_attn.py:261-269): token i of k / v ((T, 4, 128)
+ * bf16) goes to block slot_mapping[i] / ebs, row slot_mapping[i] % ebs of the [blocks, 4, ebs, 256] cache (element
+ * strides s0, s1, s2; K at + 0, V at + 128); negative slots (padding) are skipped.
+ */
+KV800_API int kv800_write_slots(uint16_t* ecache, int64_t ecache_elems, int64_t s0, int64_t s1, int64_t s2,
+                                int64_t ebs, const uint16_t* k, const uint16_t* v, const int64_t* slot_mapping,
+                                int64_t T, int* status, void* stream);
+
+/*
  * kv800_write_exact -- replaces the exact-page scatter of PagedStore.append (kv800.py:423-428) and of the vLLM
  * backend (vllm_attn.py:261-269): token i (i < T) of k / v ((T, 4, 128) bf16, contiguous) goes to sequence seq[i],
  * position pos[i]: K at epool + eoff[seq * eoff_stride + pos / ebs] + h*e_hs + (pos % ebs)*e_ts, V at + e_v.

@@ -13,6 +13,7 @@
 #include <cstdarg>
 #include <cstdio>
 
+#include "hadamard.cuh"
 #include "kv800_common.cuh"
 
 namespace kv800 {
@@ -75,6 +76,138 @@ struct PagedSrc {
     }
 };
 
+// vLLM layout (vllm_attn.py:298-317): the exact cache is [blocks, 4, ebs, 256] bf16 addressed through a block
+// table (row b of bt: block ids of request b), the quant cache is pages of qs0 bytes holding bsq / 256 sub-blocks each,
+// addressed through qbt.  Sub-block m of the launch is pair m of a device-built list (request, sub-block index); CTAs
+// past the list's count exit.
+struct VllmSrc {
+    const uint16_t* epool;
+    int64_t epool_elems, s0, s1, s2, ebs;
+    const int32_t* bt;
+    int64_t bt_stride;
+    uint8_t* qpool;
+    int64_t qpool_bytes, qs0, bsq;
+    const int32_t* qbt;
+    int64_t qbt_stride;
+    const int32_t* pairs;   // [2 * max] (request, sub-block)
+    const int32_t* count;
+    int64_t R;
+    int* status;
+    __device__ __forceinline__ bool rows(int64_t m, int t, int h, const uint16_t*& kr, const uint16_t*& vr) const {
+        const int64_t b = pairs[2 * m], j = pairs[2 * m + 1];
+        const int64_t p = j * BLK + t;
+        if (b < 0 || b >= R || p / ebs >= bt_stride) {
+            flag(status, ST_TABLE);
+            return false;
+        }
+        const int64_t blk = bt[b * bt_stride + p / ebs];
+        const int64_t o = blk * s0 + h * s1 + (p % ebs) * s2;
+        if (blk < 0 || o < 0 || o + 256 > epool_elems) {
+            flag(status, ST_EPOOL);
+            return false;
+        }
+        kr = epool + o;
+        vr = epool + o + 128;
+        return true;
+    }
+    __device__ __forceinline__ uint8_t* dst(int64_t m) const {
+        if (m >= *count) return nullptr;
+        const int64_t b = pairs[2 * m], j = pairs[2 * m + 1];
+        const int64_t tok0 = j * BLK;
+        if (b < 0 || b >= R || tok0 / bsq >= qbt_stride) {
+            flag(status, ST_TABLE);
+            return nullptr;
+        }
+        const int64_t blk = qbt[b * qbt_stride + tok0 / bsq];
+        const int64_t o = blk * qs0 + ((tok0 % bsq) / BLK) * SUB;
+        if (blk < 0 || o < 0 || o + SUB > qpool_bytes) {
+            flag(status, ST_QPOOL);
+            return nullptr;
+        }
+        return qpool + o;
+    }
+};
+
+// Flush plan of one vLLM step on the device: request b (seq_len[b] tokens after the step, qlen[b] = qsl[b + 1] -
+// qsl[b] of them new) owns sub-blocks j in [nq(seq_len[b] - qlen[b]), nq(seq_len[b])) with nq(n) = max(0, n - 128) /
+// 256, the flush rule of vllm_attn.py:303-304; they are listed in request order as (b, j) pairs, at most max_pairs
+// (more flags ST_TABLE and is cut).  One CTA of 1024 threads (block-wide scan); writes pairs [2 * max_pairs] and
+// count.
+__global__ void __launch_bounds__(1024) flush_plan_kernel(const int32_t* seq_len, const int32_t* qsl, int64_t R,
+                                                          int64_t max_pairs, int32_t* pairs, int32_t* count,
+                                                          int* status) {
+    __shared__ int64_t wsum[32];
+    __shared__ int64_t carry;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) carry = 0;
+    __syncthreads();
+    for (int64_t base = 0; base < R; base += 1024) {
+        const int64_t b = base + tid;
+        int64_t j0 = 0, n = 0;
+        if (b < R) {
+            const int64_t sl = seq_len[b], prev = sl - (int64_t)(qsl[b + 1] - qsl[b]);
+            const int64_t a0 = prev > LAG ? (prev - LAG) / BLK : 0;
+            const int64_t a1 = sl > LAG ? (sl - LAG) / BLK : 0;
+            j0 = a0;
+            n = a1 > a0 ? a1 - a0 : 0;
+        }
+        int64_t x = n;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int64_t y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) wsum[warp] = x;
+        __syncthreads();
+        if (warp == 0) {
+            int64_t w = wsum[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int64_t y = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o) w += y;
+            }
+            wsum[lane] = w;
+        }
+        __syncthreads();
+        const int64_t start = carry + (warp ? wsum[warp - 1] : 0) + x - n;
+        for (int64_t i = 0; i < n; i++) {
+            if (start + i >= max_pairs) {
+                flag(status, ST_TABLE);
+                break;
+            }
+            pairs[2 * (start + i)] = (int32_t)b;
+            pairs[2 * (start + i) + 1] = (int32_t)(j0 + i);
+        }
+        __syncthreads();
+        if (tid == 0) carry += wsum[31];
+        __syncthreads();
+    }
+    if (tid == 0) *count = (int32_t)(carry < max_pairs ? carry : max_pairs);
+}
+
+// Exact-cache scatter through vLLM's slot mapping (vllm_attn.py:261-269): token i goes to block slot[i] / ebs, row
+// slot[i] % ebs; slot < 0 (padding) is skipped.  One warp per (token, head, K|V) row.
+__global__ void write_slots_kernel(uint16_t* epool, int64_t epool_elems, int64_t s0, int64_t s1, int64_t s2,
+                                   int64_t ebs, const uint16_t* k, const uint16_t* v, const int64_t* slot, int64_t T,
+                                   int* status) {
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= T * HEADS * 2) return;
+    const int64_t i = row / (HEADS * 2);
+    const int h = (int)((row / 2) % HEADS), isv = (int)(row & 1);
+    const int64_t sl = slot[i];
+    if (sl < 0) return;
+    const int64_t o = (sl / ebs) * s0 + h * s1 + (sl % ebs) * s2 + (isv ? 128 : 0);
+    if (o < 0 || o + DIM > epool_elems) {
+        if (lane == 0) flag(status, ST_EPOOL);
+        return;
+    }
+    const uint16_t* srow = (isv ? v : k) + (i * HEADS + h) * DIM;
+    uint16_t* drow = epool + o;
+#pragma unroll
+    for (int e = 0; e < 4; e++) drow[lane * 4 + e] = srow[lane * 4 + e];
+}
+
 constexpr int VSPLIT = 4;               // V-part CTAs per sub-block (64 tokens each)
 constexpr int VTOK = BLK / VSPLIT;
 
@@ -96,53 +229,6 @@ __device__ __forceinline__ void load16(const uint16_t* row, int e, float* out) {
     }
 }
 
-
-// y[h][k] = (x_h @ H)[lane + 32 k] for the 4 rows x_h = rows[h * 128 .. h * 128 + 127] (fp32, shared memory), each
-// output the sequential chain acc = fma(x_i, H[i][d], acc), i = 0 .. 127, from acc = 0: the arithmetic of the
-// reference's CPU BLAS for v.float() @ H, so the result is bit-identical.  C[b] = +-c for the lane part of the sign
-// (parity(b & lane)); the (a, k) part of the sign, parity(a & k) for i = 32 a + b and d = lane + 32 k, is folded
-// into the operand at compile time.
-__device__ __forceinline__ void hadamard_rows(const float* rows, const float (&C)[32], float (&y)[HEADS][4]) {
-#pragma unroll
-    for (int hp = 0; hp < 2; hp++) {
-        float acc[2][4];
-#pragma unroll
-        for (int q = 0; q < 2; q++)
-#pragma unroll
-            for (int k = 0; k < 4; k++) acc[q][k] = 0.f;
-        const float* v0 = rows + (2 * hp) * DIM;
-        const float* v1 = rows + (2 * hp + 1) * DIM;
-#pragma unroll
-        for (int a = 0; a < 4; a++) {
-#pragma unroll
-            for (int b4 = 0; b4 < 32; b4 += 4) {
-                float4 x0 = *reinterpret_cast<const float4*>(v0 + 32 * a + b4);
-                float4 x1 = *reinterpret_cast<const float4*>(v1 + 32 * a + b4);
-                float xs0[4] = {x0.x, x0.y, x0.z, x0.w}, xs1[4] = {x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-#pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        const bool neg = (__builtin_popcount(a & k) & 1) != 0;
-                        acc[0][k] = fmaf(neg ? -xs0[u] : xs0[u], C[b4 + u], acc[0][k]);
-                        acc[1][k] = fmaf(neg ? -xs1[u] : xs1[u], C[b4 + u], acc[1][k]);
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            y[2 * hp][k] = acc[0][k];
-            y[2 * hp + 1][k] = acc[1][k];
-        }
-    }
-}
-
-__device__ __forceinline__ void hadamard_signs(int lane, float (&C)[32]) {
-    const float c = 0.0883883461356163f;   // fp32(1 / sqrt(128)), the entry magnitude of the reference's hadamard()
-#pragma unroll
-    for (int b = 0; b < 32; b++) C[b] = (__popc(b & lane) & 1) ? -c : c;
-}
 
 template <class Src>
 __global__ void __launch_bounds__(256) flush_kernel(Src src) {
@@ -529,4 +615,69 @@ extern "C" int kv800_fake_quant_v(const float* v, int64_t N, float* out, void* s
     }
     fake_quant_v_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(v, N, out);
     return cuda_status(cudaGetLastError(), "kv800_fake_quant_v launch");
+}
+
+extern "C" int kv800_write_slots(uint16_t* ecache, int64_t ecache_elems, int64_t s0, int64_t s1, int64_t s2,
+                                 int64_t ebs, const uint16_t* k, const uint16_t* v, const int64_t* slot_mapping,
+                                 int64_t T, int* status, void* stream) {
+    if (T < 0) {
+        set_error("kv800_write_slots: negative T");
+        return KV800_ERR_ARG;
+    }
+    if (T == 0) return KV800_OK;
+    if (!ecache || !k || !v || !slot_mapping || ebs <= 0) {
+        set_error("kv800_write_slots: null pointer or ebs <= 0");
+        return KV800_ERR_ARG;
+    }
+    const int64_t blocks = (T * HEADS * 2 + 7) / 8;
+    if (blocks > 0x7fffffffLL) {
+        set_error("kv800_write_slots: T = %lld too large", (long long)T);
+        return KV800_ERR_RANGE;
+    }
+    write_slots_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(ecache, ecache_elems, s0, s1, s2, ebs, k, v,
+                                                                       slot_mapping, T, status);
+    return cuda_status(cudaGetLastError(), "kv800_write_slots launch");
+}
+
+extern "C" int64_t kv800_flush_step_workspace_size(int64_t max_pairs) {
+    if (max_pairs < 0) return -1;
+    return 256 + ((max_pairs * 2 * 4 + 255) & ~(int64_t)255);
+}
+
+extern "C" int kv800_flush_step(const uint16_t* ecache, int64_t ecache_elems, int64_t s0, int64_t s1, int64_t s2,
+                                int64_t ebs, const int32_t* block_table, int64_t bt_stride, uint8_t* qcache,
+                                int64_t qcache_bytes, int64_t qs0, int64_t bsq, const int32_t* qblock_table,
+                                int64_t qbt_stride, const int32_t* seq_lens, const int32_t* query_start_loc, int64_t R,
+                                int64_t max_pairs, void* workspace, int64_t workspace_bytes, int* status,
+                                void* stream) {
+    if (R < 0 || max_pairs < 0) {
+        set_error("kv800_flush_step: negative R / max_pairs");
+        return KV800_ERR_ARG;
+    }
+    if (R == 0 || max_pairs == 0) return KV800_OK;
+    if (!ecache || !block_table || !qcache || !qblock_table || !seq_lens || !query_start_loc || !workspace ||
+        ebs <= 0 || bsq <= 0 || bsq % BLK || bt_stride <= 0 || qbt_stride <= 0) {
+        set_error("kv800_flush_step: null pointer, or bad ebs / bsq (a multiple of 256) / table strides");
+        return KV800_ERR_ARG;
+    }
+    const int64_t need = kv800_flush_step_workspace_size(max_pairs);
+    if (workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u)) {
+        set_error("kv800_flush_step: workspace of %lld bytes (256-aligned), %lld needed", (long long)workspace_bytes,
+                  (long long)need);
+        return KV800_ERR_RANGE;
+    }
+    if (max_pairs > 0x7fffffffLL || R > 0x7fffffffLL) {
+        set_error("kv800_flush_step: R / max_pairs above 2^31 - 1");
+        return KV800_ERR_RANGE;
+    }
+    cudaStream_t st = as_stream(stream);
+    int32_t* count = static_cast<int32_t*>(workspace);
+    int32_t* pairs = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + 256);
+    flush_plan_kernel<<<1, 1024, 0, st>>>(seq_lens, query_start_loc, R, max_pairs, pairs, count, status);
+    int rc = cuda_status(cudaGetLastError(), "kv800_flush_step plan");
+    if (rc) return rc;
+    VllmSrc src{ecache, ecache_elems, s0, s1, s2, ebs, block_table, bt_stride, qcache, qcache_bytes, qs0, bsq,
+                qblock_table, qbt_stride, pairs, count, R, status};
+    flush_kernel<VllmSrc><<<dim3((unsigned)max_pairs, 1 + VSPLIT), 256, 0, st>>>(src);
+    return cuda_status(cudaGetLastError(), "kv800_flush_step flush");
 }

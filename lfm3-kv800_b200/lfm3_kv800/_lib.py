@@ -29,6 +29,16 @@ SIGNATURES = {
     "kv800_dequantize_blocks": (_int, [_p, _i64, _p, _p, _p]),
     "kv800_fake_quant_k": (_int, [_p, _i64, _i64, _p, _p]),
     "kv800_fake_quant_v": (_int, [_p, _i64, _p, _p]),
+    "kv800_write_slots": (_int, [_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _p]),
+    "kv800_flush_step_workspace_size": (_i64, [_i64]),
+    "kv800_flush_step": (_int, [_p, _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64, _p, _i64, _p, _p,
+                                _i64, _i64, _p, _i64, _p, _p]),
+    "kv800_write_sinks": (_int, [_p, _i64, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _p, _p,
+                                 _i64, _i64, _p, _p]),
+    "kv800_decode_tables": (_int, [_p, _i64, _p, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p,
+                                   _p, _i64, _i64, _i64, _p, _p, _i64, _i64, _i64, _p, _p]),
+    "kv800_prefill_kv": (_int, [_p, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i64,
+                                _p, _i64, _i64, _i64, _p, _p, _i64, _p, _p, _i64, _p, _p, _p, _p]),
     "kv800_flush": (_int, [_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _i64, _p, _p, _i64, _i64, _p,
                            _p]),
     "kv800_write_exact": (_int, [_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p]),

@@ -62,6 +62,45 @@ def test_host_argument_checks():
     assert L.kv800_check_status(None, None, None) == _lib.ERR_ARG
 
 
+def test_step_entry_argument_checks():
+    """The vLLM-step entry points reject bad arguments on the host and treat empty work as a no-op."""
+    L = _lib.lib()
+    # write_slots: negative T, empty, null pointers
+    assert L.kv800_write_slots(None, 0, 0, 0, 0, 64, None, None, None, -1, None, None) == _lib.ERR_ARG
+    assert L.kv800_write_slots(None, 0, 0, 0, 0, 64, None, None, None, 0, None, None) == _lib.OK
+    assert L.kv800_write_slots(None, 0, 0, 0, 0, 64, None, None, None, 5, None, None) == _lib.ERR_ARG
+    # flush_step: workspace sizing, nothing to flush, bad bsq, short workspace
+    assert L.kv800_flush_step_workspace_size(0) == 256
+    assert L.kv800_flush_step_workspace_size(3) == 512
+    assert L.kv800_flush_step_workspace_size(-1) == -1
+    args = [None, 0, 0, 0, 0, 64, None, 1, None, 0, 262144, 1280, None, 1, None, None]
+    assert L.kv800_flush_step(*args, 4, 0, None, 0, None, None) == _lib.OK
+    assert L.kv800_flush_step(*args, 4, 2, None, 0, None, None) == _lib.ERR_ARG
+    fake = ctypes.c_void_p(256)        # never dereferenced: every check below fails before a launch
+    good = [fake, 0, 0, 0, 0, 64, fake, 1, fake, 0, 262144, 1280, fake, 1, fake, fake]
+    bad_bsq = list(good)
+    bad_bsq[11] = 1000
+    assert L.kv800_flush_step(*bad_bsq, 4, 2, fake, 4096, None, None) == _lib.ERR_ARG
+    assert L.kv800_flush_step(*good, 4, 2, fake, 16, None, None) == _lib.ERR_RANGE
+    assert b"workspace" in L.kv800_last_error()
+    # write_sinks / decode_tables / prefill_kv
+    assert L.kv800_write_sinks(*[None, 0, 0, 0, None, 0] * 2, None, None, None, None, None, 2, -1, None, None) == _lib.ERR_ARG
+    assert L.kv800_write_sinks(*[None, 0, 0, 0, None, 0] * 2, None, None, None, None, None, 2, 0, None, None) == _lib.OK
+    tab = [None, 0, 0, 0, None] * 2
+    assert L.kv800_decode_tables(None, 0, None, 0, 0, None, None, None, None, 0, 0, 0, 0, None, *tab, None) == _lib.OK
+    assert L.kv800_decode_tables(None, 3, None, 0, 0, None, None, None, None, 0, 0, 0, 0, None, *tab, None) == _lib.ERR_ARG
+    assert L.kv800_decode_tables(fake, 3, fake, 4, 0, fake, fake, fake, None, 0, 0, 1280, 5, fake, *tab,
+                                 None) == _lib.ERR_ARG
+    assert b"quant block table" in L.kv800_last_error()
+    none_pf = [None, 0, 0, 0, None, 0]
+    assert L.kv800_prefill_kv(*none_pf, 0, None, None, 5, *[None, 0, 0, 0, 0, 0, None, 0], 0, 0, None, None, 0,
+                              None, None, 0, None, None, None, None) == _lib.ERR_ARG                  # ns > 4
+    assert L.kv800_prefill_kv(*none_pf, 0, None, None, 0, *[None, 0, 0, 0, 0, 0, None, 0], 0, 0, None, None, 0,
+                              None, None, 0, None, None, None, None) == _lib.OK                       # nothing
+    assert L.kv800_prefill_kv(*none_pf, 2, None, None, 0, *[None, 0, 0, 0, 0, 0, None, 0], 0, 0, None, None, 0,
+                              None, None, 0, fake, fake, None, None) == _lib.ERR_ARG                  # no quant cache
+
+
 def _plan_bytes(B, nqmax, win, spb, G0=444):
     up = lambda x: (x + 255) & ~255
     nq = 0 if win else nqmax

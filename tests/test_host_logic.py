@@ -76,3 +76,25 @@ def test_paged_slots():
     assert P.win == 256 and P.nqmax == 3 and P.sk is None
     assert set(kv800.Paged.__slots__) == {"qpool", "boff", "epool", "eoff", "ebs", "e_hs", "e_ts", "e_v", "sk", "sv",
                                           "skoff", "svoff", "N", "NQ", "nqmax", "win"}
+
+
+def test_vllm_step_host_values():
+    """Host values of a vLLM step come from the CPU copies of the metadata: the flushed sub-block count (the flush
+    rule n >= 256 j + 384 between the lengths before and after the step) and the positions of the scheduled tokens."""
+    import torch
+    from lfm3_kv800 import vllm_step as S
+    assert [S.nq_of(n) for n in (0, 383, 384, 639, 640, 1151, 1152)] == [0, 0, 1, 1, 2, 3, 4]
+    sl = torch.tensor([1151, 384, 2000, 5], dtype=torch.int32)
+    qsl = torch.tensor([0, 1, 2, 2002, 2007], dtype=torch.int32)    # decodes, a 2000-token prefill, a 5-token prefill
+    # prev = 1150, 383, 0, 0 -> flushes 3-3, 1-0, 7-0, 0
+    assert S.flush_pairs(sl, qsl) == 0 + 1 + 7 + 0
+    m = S.build_meta(torch.zeros(4, 16, dtype=torch.int32), torch.arange(2007), sl, qsl, sl, qsl)
+    assert m.num_decodes == 2 and m.num_reqs == 4 and m.num_actual_tokens == 2007
+    pos = m.positions.numpy()
+    assert pos[0] == 1150 and pos[1] == 383 and list(pos[2:5]) == [0, 1, 2] and pos[2001] == 1999
+    assert list(pos[2002:]) == [0, 1, 2, 3, 4]
+    qv = torch.zeros(3 * S.QPAGE, dtype=torch.uint8)
+    view = torch.as_strided(qv, (3, 2, S.QBLOCK, 4, S.QCONTENT), (S.QPAGE, 128000, 100, 25, 1))
+    assert S.aux_offset(view) == 5 * 25600                              # bf16 elements: after 5 sub-blocks
+    flat, ps = S.bf16_flat(view[1:])
+    assert ps == S.QPAGE // 2 and flat.numel() == 2 * S.QPAGE // 2 and flat.dtype == torch.bfloat16
