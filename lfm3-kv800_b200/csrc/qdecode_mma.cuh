@@ -94,9 +94,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
 
 // bf16 bits of an fp8 e4m3fn byte scaled by 2^e (exact for the scalings used here).
 __device__ __forceinline__ uint32_t f8_to_bf16_scaled(uint32_t b, float pw2) {
@@ -218,24 +215,20 @@ __device__ __forceinline__ int swz(int c) { return (c & ~7) | ((c & 7) ^ ((c >> 
 
 // copy half `half` of the sub-block at src into a stage: kc rows, vb lines (both swizzled), and for half 0 the scales
 __device__ __forceinline__ void stage_half(uint8_t* dst, const uint8_t* src, int half, int tid) {
-    const uint32_t d0 = smem_u32(dst);
-    const int nck = QM_KC_BYTES / 16, ncv = QM_VB_BYTES / 16, ncs = half ? 0 : QM_SC_BYTES / 16;
-    for (int c = tid; c < nck + ncv + ncs; c += 128) {
-        int so, dof;
-        if (c < nck) {
-            so = half * QM_KC_BYTES + 16 * c;
-            dof = 16 * swz(c);
-        } else if (c < nck + ncv) {
-            const int r = c - nck;
-            so = VB_O + half * QM_VB_BYTES + 16 * r;
-            dof = ST_VB + 16 * swz(r);
-        } else {
-            const int r = c - nck - ncv;
-            so = VLO_O + 16 * r;
-            dof = ST_SC + 16 * r;
-        }
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d0 + dof), "l"(src + so) : "memory");
-    }
+    // 128 threads: 8 kc chunks, 4 vb chunks and (half 0) one scale chunk each; chunk tid + 128 r swizzles to
+    // swz(tid) + 128 r, so every copy is a fixed offset from two per-thread bases
+    const uint32_t dk = smem_u32(dst) + 16 * swz(tid);
+    const uint8_t* sk = src + half * QM_KC_BYTES + 16 * tid;
+#pragma unroll
+    for (int r = 0; r < QM_KC_BYTES / 16 / 128; r++)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk + 2048 * r), "l"(sk + 2048 * r) : "memory");
+    const uint8_t* sv = src + VB_O + half * QM_VB_BYTES + 16 * tid;
+#pragma unroll
+    for (int r = 0; r < QM_VB_BYTES / 16 / 128; r++)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk + ST_VB + 2048 * r), "l"(sv + 2048 * r) : "memory");
+    if (half == 0)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst) + ST_SC + 16 * tid),
+                     "l"(src + VLO_O + 16 * tid) : "memory");
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
@@ -465,27 +458,15 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
             __syncthreads();
         }
         if (ok) {
-            DequantConsts K;
-            {
-                const uint4* cp = reinterpret_cast<const uint4*>(cst);
-#pragma unroll
-                for (int p = 0; p < 4; p++) {
-                    const uint4 w0 = cp[((h * 4 + p) * 4 + tig) * 2];
-                    const uint4 w1 = cp[((h * 4 + p) * 4 + tig) * 2 + 1];
-                    K.A[p][0] = w0.x; K.L[p][0] = w0.y; K.A[p][1] = w0.z; K.L[p][1] = w0.w;
-                    K.A[p][2] = w1.x; K.L[p][2] = w1.y; K.A[p][3] = w1.z; K.L[p][3] = w1.w;
-                }
-            }
+            // dequant constants stay in shared memory and are re-read for every 16-token tile (8 x 16 B per thread):
+            // holding them in registers across the tile loop costs more in spills than the loads
+            const uint4* cstp = reinterpret_cast<const uint4*>(cst);
             const int64_t pos0 = jb * BLK + half * QM_HALF;   // position of the half's first token
             const float2* vslh = vsl + 2 * half * QM_HALF;
-            // cos / sin rows of the tile's tokens t0 + g and t0 + g + 8 (this thread's 8 frequencies): loaded one
-            // 16-token tile ahead so the L2 latency of the table overlaps the previous tile's work
+            // cos / sin rows of the tile's tokens t0 + g and t0 + g + 8 (this thread's 8 frequencies; the 4 warps
+            // read the same rows, served by L1)
             const uint16_t* crow0 = a.cos_t + (pos0 + g) * 32 + 8 * tig;
             const uint16_t* srow0 = a.sin_t + (pos0 + g) * 32 + 8 * tig;
-            uint4 pf_ca = *reinterpret_cast<const uint4*>(crow0);
-            uint4 pf_sa = *reinterpret_cast<const uint4*>(srow0);
-            uint4 pf_cb = *reinterpret_cast<const uint4*>(crow0 + 8 * 32);
-            uint4 pf_sb = *reinterpret_cast<const uint4*>(srow0 + 8 * 32);
 #pragma unroll 1
             for (int c0 = 0; c0 < QM_HALF; c0 += 32) {
                 float sc[2][4];
@@ -498,14 +479,19 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
                         const uint8_t* kt = raw + t0 * 128;
                         const uint2 kwa = *reinterpret_cast<const uint2*>(kt + koff_a);
                         const uint2 kwb = *reinterpret_cast<const uint2*>(kt + koff_b);
-                        const uint4 ca = pf_ca, sa = pf_sa, cb = pf_cb, sbw = pf_sb;
-                        if (t0 + 16 < QM_HALF) {
-                            const uint16_t* crow = crow0 + (t0 + 16) * 32;
-                            const uint16_t* srow = srow0 + (t0 + 16) * 32;
-                            pf_ca = *reinterpret_cast<const uint4*>(crow);
-                            pf_sa = *reinterpret_cast<const uint4*>(srow);
-                            pf_cb = *reinterpret_cast<const uint4*>(crow + 8 * 32);
-                            pf_sb = *reinterpret_cast<const uint4*>(srow + 8 * 32);
+                        const uint16_t* crow = crow0 + t0 * 32;
+                        const uint16_t* srow = srow0 + t0 * 32;
+                        const uint4 ca = *reinterpret_cast<const uint4*>(crow);
+                        const uint4 sa = *reinterpret_cast<const uint4*>(srow);
+                        const uint4 cb = *reinterpret_cast<const uint4*>(crow + 8 * 32);
+                        const uint4 sbw = *reinterpret_cast<const uint4*>(srow + 8 * 32);
+                        DequantConsts K;
+#pragma unroll
+                        for (int p = 0; p < 4; p++) {
+                            const uint4 w0 = cstp[((h * 4 + p) * 4 + tig) * 2];
+                            const uint4 w1 = cstp[((h * 4 + p) * 4 + tig) * 2 + 1];
+                            K.A[p][0] = w0.x; K.L[p][0] = w0.y; K.A[p][1] = w0.z; K.L[p][1] = w0.w;
+                            K.A[p][2] = w1.x; K.L[p][2] = w1.y; K.A[p][3] = w1.z; K.L[p][3] = w1.w;
                         }
                         token_regs(kwa.x, kwa.y, ca, sa, K, R0);
                         token_regs(kwb.x, kwb.y, cb, sbw, K, R1);
