@@ -228,10 +228,41 @@ static int qdecode_setup() {
 static int xdecode_setup() {
     static int done = 0;
     if (!done) {
-        int rc = cuda_status(cudaFuncSetAttribute(xdecode_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, XM_SMEM),
+        int rc = cuda_status(cudaFuncSetAttribute(xdecode_mma<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  XM_SMEM),
                              "xdecode_mma smem attribute");
         if (rc) return rc;
+        rc = cuda_status(cudaFuncSetAttribute(xdecode_mma<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, XM_SMEM),
+                         "xdecode_mma smem attribute");
+        if (rc) return rc;
         done = 1;
+    }
+    return KV800_OK;
+}
+
+// Launch the exact-token partials: with tables, or (both tables null) the no-rotation form of native sliding layers.
+static void launch_xdecode(const XMArgs& xa, dim3 grid, cudaStream_t st) {
+    if (xa.cos_t) xdecode_mma<true><<<grid, 128, XM_SMEM, st>>>(xa);
+    else xdecode_mma<false><<<grid, 128, XM_SMEM, st>>>(xa);
+}
+
+// Tables: both given (16-byte aligned, npos > 0), or both null when nothing quantized is decoded (no rotation).
+static int check_tables(const uint16_t* cos_t, const uint16_t* sin_t, int64_t npos, bool quantized, const char* who) {
+    if (!cos_t && !sin_t) {
+        if (quantized) {
+            set_error("%s: quantized sub-blocks need the cos / sin tables (null tables mean no rotation, for layers "
+                      "without quantized sub-blocks only)", who);
+            return KV800_ERR_ARG;
+        }
+        return KV800_OK;
+    }
+    if (!cos_t || !sin_t || npos <= 0) {
+        set_error("%s: give both cos / sin tables with npos > 0, or neither", who);
+        return KV800_ERR_ARG;
+    }
+    if ((reinterpret_cast<uintptr_t>(cos_t) | reinterpret_cast<uintptr_t>(sin_t)) & 15u) {
+        set_error("%s: cos / sin tables must be 16-byte aligned", who);
+        return KV800_ERR_ARG;
     }
     return KV800_OK;
 }
@@ -246,14 +277,12 @@ extern "C" int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint1
         return B < 0 ? KV800_ERR_ARG : KV800_ERR_RANGE;
     }
     if (B == 0) return KV800_OK;
-    if (!q || !cos_t || !sin_t || !out || !workspace || npos <= 0) {
-        set_error("kv800_decode: null q / cos / sin / out / workspace or npos <= 0");
+    if (!q || !out || !workspace) {
+        set_error("kv800_decode: null q / out / workspace");
         return KV800_ERR_ARG;
     }
-    if ((reinterpret_cast<uintptr_t>(cos_t) | reinterpret_cast<uintptr_t>(sin_t)) & 15u) {
-        set_error("kv800_decode: cos / sin tables must be 16-byte aligned");
-        return KV800_ERR_ARG;
-    }
+    rc = check_tables(cos_t, sin_t, npos, P->win == 0 && P->nqmax > 0, "kv800_decode");
+    if (rc) return rc;
     if (reinterpret_cast<uintptr_t>(q) & 15u) {
         set_error("kv800_decode: q must be 16-byte aligned");
         return KV800_ERR_ARG;
@@ -322,7 +351,7 @@ extern "C" int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint1
     rc = xdecode_setup();
     if (rc) return rc;
     XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, sm.xbase, sm.xstride, NX_DEFAULT, SCALE, status};
-    xdecode_mma<<<dim3((unsigned)B, (unsigned)NX_DEFAULT), 128, XM_SMEM, st>>>(xa);
+    launch_xdecode(xa, dim3((unsigned)B, (unsigned)NX_DEFAULT), st);
     rc = cuda_status(cudaGetLastError(), "kv800_decode xdecode");
     if (rc) return rc;
     combine_kernel<<<(unsigned)B, 512, 0, st>>>(mo, lo, ao, sm, out);
@@ -368,10 +397,12 @@ extern "C" int kv800_xdecode(const uint16_t* q, const kv800_paged* P, const uint
         return KV800_ERR_ARG;
     }
     if (B == 0) return KV800_OK;
-    if (!q || !cos_t || !sin_t || !mo || !lo || !ao) {
+    if (!q || !mo || !lo || !ao) {
         set_error("kv800_xdecode: null pointer");
         return KV800_ERR_ARG;
     }
+    rc = check_tables(cos_t, sin_t, npos, false, "kv800_xdecode");
+    if (rc) return rc;
     if (reinterpret_cast<uintptr_t>(ao) & 15u) {
         set_error("kv800_xdecode: ao must be 16-byte aligned");
         return KV800_ERR_ARG;
@@ -383,7 +414,7 @@ extern "C" int kv800_xdecode(const uint16_t* q, const kv800_paged* P, const uint
     int rcx = xdecode_setup();
     if (rcx) return rcx;
     XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, ns, ns + 1, 1, scale, status};
-    xdecode_mma<<<dim3((unsigned)B, 1), 128, XM_SMEM, as_stream(stream)>>>(xa);
+    launch_xdecode(xa, dim3((unsigned)B, 1), as_stream(stream));
     return cuda_status(cudaGetLastError(), "kv800_xdecode launch");
 }
 

@@ -12,6 +12,9 @@
 //            movmatrix, split into bf16 hi + lo (P - hi) so the products keep ~16 bits of P; fp32 accumulate.
 // Online softmax in the log2 domain with a lazily moved reference point (as in qdecode_mma).  The partial (m, l, acc)
 // goes to slot xbase + b xstride + e (the reference's slot ns of row b for the single-split form, kv800.py:224-228).
+// ROPE = false is the native sliding layers' form (keys stored post-RoPE, vllm_attn.py:256-257): the reference passes
+// all-ones / all-zeros tables there, whose rotation returns every key unchanged, so this form drops the table copies
+// and the rotation and gives the same scores.
 #pragma once
 #include "qdecode_mma.cuh"
 
@@ -74,6 +77,7 @@ __device__ __forceinline__ void rope_frag(uint32_t& k0, uint32_t& k2, uint32_t c
 // smem byte offset of (row r, 16-byte chunk c) in a [16 rows][256 B] swizzled tile
 __device__ __forceinline__ int xm_off(int r, int c) { return r * 256 + ((c ^ (r & 7)) << 4); }
 
+template <bool ROPE>
 __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int b = blockIdx.x, e = blockIdx.y, tid = threadIdx.x;
@@ -137,7 +141,7 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
                     flag(a.status, ST_TABLE);
                 }
             }
-            if (ok && pos >= a.npos) {
+            if (ROPE && ok && pos >= a.npos) {
                 if (sub == 0) flag(a.status, ST_TABLE);
                 ok = false;
             }
@@ -150,7 +154,7 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
 #pragma unroll
         for (int c = 0; c < 16; c++) cp16(dst + xm_off(tt, c), ok ? (const void*)(row + 8 * c) : (const void*)P.epool, ok);
         // cos / sin rows: token tid / 8 ... one chunk per thread
-        {
+        if (ROPE) {
             const int tc = tid >> 3, which = (tid >> 2) & 1, c4 = tid & 3;
             const int64_t tj = (int64_t)it * XM_TILE + tc;
             int64_t pj = -1;
@@ -206,14 +210,16 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
         }
         // RoPE on K-steps 0,1 (dims 0..31) with 4,5 (dims 64..95): regs 0 / 2 are token g, 1 / 3 token g + 8;
         // regs 0 / 1 cover dims 16 ks + 2 tig, regs 2 / 3 dims 16 ks + 8 + 2 tig
+        if (ROPE) {
 #pragma unroll
-        for (int ks = 0; ks < 2; ks++)
+            for (int ks = 0; ks < 2; ks++)
 #pragma unroll
-            for (int rg = 0; rg < 4; rg++) {
-                const int tok = g + 8 * (rg & 1);
-                const int d = 16 * ks + 8 * (rg >> 1) + 2 * tig;   // even, < 32
-                rope_frag(A[ks][rg], A[ks + 4][rg], cs[tok * 16 + (d >> 1)], sn[tok * 16 + (d >> 1)]);
-            }
+                for (int rg = 0; rg < 4; rg++) {
+                    const int tok = g + 8 * (rg & 1);
+                    const int d = 16 * ks + 8 * (rg >> 1) + 2 * tig;   // even, < 32
+                    rope_frag(A[ks][rg], A[ks + 4][rg], cs[tok * 16 + (d >> 1)], sn[tok * 16 + (d >> 1)]);
+                }
+        }
         float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int ks = 0; ks < 8; ks++) mma_bf16(sc, A[ks][0], A[ks][1], A[ks][2], A[ks][3], bq[ks][0], bq[ks][1]);

@@ -272,7 +272,8 @@ def _paged_struct(P, dev, B):
 
 def decode(P, q, cos_t, sin_t, H=None, spb=None, target=None):
     """q: (B, 16, 128) bf16 post-RoPE -> (B, 16, 128) bf16. cos_t / sin_t: (P, 32) bf16 tables of the 32 rotating
-    frequencies (dims d and d + 64 share frequency d, d < 32); H: accepted for signature compatibility (the kernels
+    frequencies (dims d and d + 64 share frequency d, d < 32), or both None for a layer without quantized sub-blocks
+    whose keys need no rotation (native sliding layers); H: accepted for signature compatibility (the kernels
     apply the normalized 128-point Hadamard themselves).  spb: sub-blocks per split; target: the reference's split
     sizing knob (spb = ceil(nqmax * B * 4 / target)); both None = the library's choice for 148 SMs."""
     _cuda(q, "decode")
@@ -286,11 +287,18 @@ def decode(P, q, cos_t, sin_t, H=None, spb=None, target=None):
     out = torch.empty(B, 16, 128, dtype=torch.bfloat16, device=dev)
     if B == 0:
         return out
-    cs, sn = _bf16(cos_t), _bf16(sin_t)
-    if cs.dim() != 2 or cs.shape[1] != 32 or sn.shape != cs.shape:
-        raise ValueError(f"decode: cos_t / sin_t must be (P, 32), got {tuple(cs.shape)} / {tuple(sn.shape)}")
-    for name, t in (("epool", P.epool), ("cos_t", cs), ("sin_t", sn)):
-        _cuda(t, f"decode ({name})")
+    if cos_t is None and sin_t is None:
+        # native sliding layers: keys stored post-RoPE, no rotation (the reference passes identity tables there)
+        cs = sn = None
+        npos = 0
+    else:
+        cs, sn = _bf16(cos_t), _bf16(sin_t)
+        if cs.dim() != 2 or cs.shape[1] != 32 or sn.shape != cs.shape:
+            raise ValueError(f"decode: cos_t / sin_t must be (P, 32), got {tuple(cs.shape)} / {tuple(sn.shape)}")
+        for name, t in (("cos_t", cs), ("sin_t", sn)):
+            _cuda(t, f"decode ({name})")
+        npos = cs.shape[0]
+    _cuda(P.epool, "decode (epool)")
     s, keep = _paged_struct(P, dev, B)
     nqmax = s.nqmax
     if spb is None and target is not None and nqmax:
@@ -298,7 +306,7 @@ def decode(P, q, cos_t, sin_t, H=None, spb=None, target=None):
     spb = int(spb or 0)
     ws_bytes = int(_lib.lib().kv800_decode_workspace_size(B, nqmax, s.win, spb))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-    _lib.call("kv800_decode", ctypes.byref(s), _ptr(q), _ptr(cs), _ptr(sn), cs.shape[0], B, spb, _ptr(out),
+    _lib.call("kv800_decode", ctypes.byref(s), _ptr(q), _ptr(cs), _ptr(sn), npos, B, spb, _ptr(out),
               _ptr(ws), ws_bytes, _stream(dev))
     _check_status(ws[:4].view(torch.int32), dev, "decode")
     del keep

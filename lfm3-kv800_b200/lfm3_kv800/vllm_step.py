@@ -342,7 +342,8 @@ class KV800Attention:
                 tb = C[tkey]
                 P = kv800.Paged(qpool=qv, boff=tb.get("boff"), epool=ev, eoff=tb["eoff"], ebs=ebs, e_hs=s1, e_ts=s2,
                                 e_v=128, N=tb["N"], NQ=tb["NQ"], nqmax=tb["nqmax"], win=0)
-            out[:nd] = kv800.decode(P, q[:nd].contiguous(), c32, s32)
+            rot = (None, None) if self.slide else (c32, s32)     # sliding layers: no rotation at all
+            out[:nd] = kv800.decode(P, q[:nd].contiguous(), *rot)
         # 4. prefill / extend rows
         qsl, sl = mx.query_start_loc_cpu, mx.seq_lens_cpu
         for i in range(nd, R):

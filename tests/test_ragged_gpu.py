@@ -119,3 +119,24 @@ def test_persistent_many_rows():
     cs, sn = I.rope_tables(1200)
     out = kv800.decode(to_dev(kv800, P), tb(q, DEV), tb(cs, DEV), tb(sn, DEV))
     assert_parity_ulp(nb(out), O.decode(P, q, cs, sn), "400 short rows")
+
+
+@pytest.mark.parametrize("sinks", [True, False])
+def test_sliding_layer_without_tables(sinks):
+    """Native sliding layers (keys stored post-RoPE) decode without tables: bit-identical to the reference's way of
+    running them, all-ones / all-zeros tables (vllm_attn.py:256-257), and within the bar of the oracle with those
+    tables.  Quantized layers still refuse null tables."""
+    from lfm3_kv800 import kv800
+    P, q = build(LENGTHS, 256, seed=23)
+    if not sinks:
+        P["sk"] = P["sv"] = None
+    one = I.f32_to_bf16(np.ones((5200, 32), np.float32))
+    zero = I.f32_to_bf16(np.zeros((5200, 32), np.float32))
+    Pd = to_dev(kv800, P)
+    got = nb(kv800.decode(Pd, tb(q, DEV), None, None))
+    ident = nb(kv800.decode(Pd, tb(q, DEV), tb(one, DEV), tb(zero, DEV)))
+    assert np.array_equal(got, ident), "no-rotation decode differs from identity tables"
+    assert_parity_ulp(got, O.decode(P, q, one, zero), f"sliding layer sinks={sinks}")
+    Pq, qq = build([900, 2000], 0, seed=3)
+    with pytest.raises(ValueError):
+        kv800.decode(to_dev(kv800, Pq), tb(qq, DEV), None, None)
