@@ -323,7 +323,7 @@ extern "C" int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint1
         rc = cuda_status(cudaGetLastError(), "kv800_decode schedule");
         if (rc) return rc;
         QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
-                  mo, lo, ao, 0, 0, SCALE, status, prefix, B};
+                  mo, lo, ao, 0, 0, SCALE, status, prefix, B, 0x40804080u, 0x38003800u};
         qdecode_mma<<<(unsigned)pl.G0, 128, QM_SMEM, st>>>(qa);
         rc = cuda_status(cudaGetLastError(), "kv800_decode qdecode");
         if (rc) return rc;
@@ -338,7 +338,7 @@ extern "C" int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint1
             rc = qdecode_setup();
             if (rc) return rc;
             QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
-                      mo, lo, ao, (int)rowslots, (int)spb, SCALE, status, nullptr, B};
+                      mo, lo, ao, (int)rowslots, (int)spb, SCALE, status, nullptr, B, 0x40804080u, 0x38003800u};
             qdecode_mma<<<dim3((unsigned)B, (unsigned)pl.ns), 128, QM_SMEM, st>>>(qa);
             rc = cuda_status(cudaGetLastError(), "kv800_decode qdecode");
             if (rc) return rc;
@@ -382,7 +382,7 @@ extern "C" int kv800_qdecode(const uint16_t* q, const uint8_t* qpool, int64_t qp
     int rc0 = qdecode_setup();
     if (rc0) return rc0;
     QMArgs qa{q, qpool, qpool_bytes, boff, boff_stride, NQ, nqmax, cos_t, sin_t, npos,
-              mo, lo, ao, (int)(ns + 1), (int)spb, scale, status, nullptr, B};
+              mo, lo, ao, (int)(ns + 1), (int)spb, scale, status, nullptr, B, 0x40804080u, 0x38003800u};
     qdecode_mma<<<dim3((unsigned)B, (unsigned)ns), 128, QM_SMEM, as_stream(stream)>>>(qa);
     return cuda_status(cudaGetLastError(), "kv800_qdecode launch");
 }

@@ -43,6 +43,10 @@ struct QMArgs {
     // prefix[B] = W) and writes the partial of its segment of row b at slot c + b.
     const int64_t* prefix;
     int64_t B;
+    // bf16x2 (4, 4) and fp16x2 (0.5, 0.5), the bases of the code encodings.  Passed as values: as compile-time
+    // constants they become immediates that the packed-half instructions cannot encode next to the LOP3's mask, and
+    // the compiler re-materializes them with an extra ALU instruction per use (~30 % of the kernel's ALU work).
+    uint32_t kbase, vbase;
 };
 
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t orv) { return (a & mask) | orv; }
@@ -165,8 +169,8 @@ __device__ __forceinline__ void rope_pairs(uint32_t k0, uint32_t k2, uint32_t ca
 }
 
 __device__ __forceinline__ void token_regs(uint32_t w0, uint32_t w1, const uint4& cw, const uint4& sw,
-                                           const DequantConsts& K, uint32_t (&R)[16]) {
-    const uint32_t BASE = 0x40804080u;   // bf16x2 (4.0, 4.0)
+                                           const DequantConsts& K, uint32_t (&R)[16], uint32_t BASE) {
+    // BASE = bf16x2 (4.0, 4.0) from the kernel arguments
     // pair words: byte pair (j, j + 2) at bits 0-7 / 16-23
     const uint32_t pw[4] = {w0, w0 >> 8, w1, w1 >> 8};
     const uint32_t cwv[4] = {cw.x, cw.y, cw.z, cw.w};   // cos of j = 8tig + {0,1}, {2,3}, {4,5}, {6,7}
@@ -493,8 +497,8 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
                             K.A[p][0] = w0.x; K.L[p][0] = w0.y; K.A[p][1] = w0.z; K.L[p][1] = w0.w;
                             K.A[p][2] = w1.x; K.L[p][2] = w1.y; K.A[p][3] = w1.z; K.L[p][3] = w1.w;
                         }
-                        token_regs(kwa.x, kwa.y, ca, sa, K, R0);
-                        token_regs(kwb.x, kwb.y, cb, sbw, K, R1);
+                        token_regs(kwa.x, kwa.y, ca, sa, K, R0, a.kbase);
+                        token_regs(kwb.x, kwb.y, cb, sbw, K, R1, a.kbase);
                     }
                     // two accumulator chains (even / odd K-steps) halve the dependent-MMA latency
                     float sx[4] = {0.f, 0.f, 0.f, 0.f}, sy[4] = {0.f, 0.f, 0.f, 0.f};
@@ -574,10 +578,10 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
 #pragma unroll
                     for (int i0 = 0; i0 < 8; i0++) {
                         const uint32_t msk = 0x00080008u << i0;
-                        mma_f16(acc[i0], lop3_and_or(wa, msk, 0x38003800u), lop3_and_or(wb, msk, 0x38003800u),
-                                lop3_and_or(wc, msk, 0x38003800u), lop3_and_or(wd, msk, 0x38003800u), b0, b1);
+                        mma_f16(acc[i0], lop3_and_or(wa, msk, a.vbase), lop3_and_or(wb, msk, a.vbase),
+                                lop3_and_or(wc, msk, a.vbase), lop3_and_or(wd, msk, a.vbase), b0, b1);
                     }
-                    mma_f16(acc[8], 0x38003800u, 0x38003800u, 0x38003800u, 0x38003800u, b0, b1);
+                    mma_f16(acc[8], a.vbase, a.vbase, a.vbase, a.vbase, b0, b1);
                 }
             }
         }
