@@ -194,14 +194,14 @@ def cpu_sample(layers, qs, c32, s32, S, reps=1):
                  svoff=None if L.skoff is None else L.skoff[:S].cpu().numpy(), N=L.N[:S].cpu().numpy(),
                  NQ=L.NQ[:S].cpu().numpy(), nqmax=L.nq, win=L.win)
         per_layer.append((P, nb(q[:S])))
-    best = None
+    ts = []
     for _ in range(reps):
         t0 = time.perf_counter()
         for P, q in per_layer:
             O.decode(P, q, cs, sn)
-        dt = time.perf_counter() - t0
-        best = dt if best is None else min(best, dt)
-    return S / best, best
+        ts.append(time.perf_counter() - t0)
+    med = statistics.median(ts)
+    return S / med, med
 
 
 # ---------------------------------------------------------------- flush / quantize (config 2)
@@ -263,10 +263,11 @@ def flush_bench(kv800, torch, dev, reps=10):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="cuda", choices=("cuda", "reference"))
-    ap.add_argument("--cpu-seqs", type=int, default=8, help="sequences of the CPU-baseline sample")
+    ap.add_argument("--cpu-seqs", type=int, default=64, help="sequences of the CPU-baseline sample")
+    ap.add_argument("--cpu-reps", type=int, default=3, help="passes of the CPU-baseline sample (median)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-flush", action="store_true", help="skip the quantize / flush measurement")
@@ -322,29 +323,34 @@ def main():
     value = a.seqs * a.steps * n_gpus / t
     launches_per_step = sum(4 if L.nq else 2 for L in layers)   # qsched + qdecode + xdecode + combine
 
-    # ---- dominant kernel alone: the decode of one quantized layer (qsched + qdecode_mma + xdecode_mma + combine;
-    # qdecode_mma is ~90 % of it by the ncu launch list), L2 flushed before every timed launch
+    # ---- dominant kernel: qdecode_mma (87.5 % of the decode kernels' device time in the ncu launch list), timed by
+    # CUDA events around the quantized phase of one quantized-layer decode (schedule + qdecode_mma) with L2 flushed
+    # before every launch; algorithmic bytes = the layer's sub-blocks read once, 64 x 127 x 51,200 B
     L0, q0 = layers[0], qs[0]
     kreps = 10
     flushbuf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     for _ in range(3):
         kv800.decode(L0.P, q0, c32, s32)
-    kt = []
+    kt, lt = [], []
     for _ in range(kreps):
         flushbuf.fill_(1)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        kv800.decode(L0.P, q0, c32, s32)
-        e1.record()
-        torch.cuda.synchronize()
-        kt.append(e0.elapsed_time(e1) / 1e3)
-    kdur = statistics.median(kt)
-    kbytes = L0.algo_bytes()
+        _, ms = kv800.decode_timed(L0.P, q0, c32, s32)
+        kt.append(ms["quantized_ms"] / 1e3)
+        lt.append((ms["quantized_ms"] + ms["exact_ms"] + ms["combine_ms"]) / 1e3)
+    kdur, ldur = statistics.median(kt), statistics.median(lt)
+    kbytes = L0.B * L0.nq * SUB
     hbm, peak_kind = peaks()
+    # DRAM traffic of qdecode_mma from one ncu capture on 64 x 16,384 (4,032 sub-blocks: 209.0 MB read + 5.5 MB
+    # written), scaled to this launch by sub-blocks (traffic grows in proportion: reads are the sub-blocks plus
+    # the cos / sin rows, writes the split partials)
+    traffic = round((209.0e6 + 5.5e6) * (L0.B * L0.nq) / 4032) if a.ctx == N_CTX and a.seqs == B_PER_GPU else None
     roofline = {"bound": "hbm", "achieved": round(kbytes / kdur / 1e9, 1), "peak": hbm, "unit": "GB/s",
-                "frac": round(kbytes / kdur / 1e9 / hbm, 4), "traffic": None, "peak_source": peak_kind,
-                "kernel": "quantized-layer decode (qdecode_mma dominant)", "bytes_per_launch": kbytes,
-                "launch_us": round(kdur * 1e6, 1)}
+                "frac": round(kbytes / kdur / 1e9 / hbm, 4), "traffic": traffic, "peak_source": peak_kind,
+                "kernel": "qdecode_mma (+ its 1-CTA schedule scan)", "bytes_per_launch": kbytes,
+                "launch_us": round(kdur * 1e6, 1),
+                "layer_decode": {"bytes": L0.algo_bytes(), "us": round(ldur * 1e6, 1),
+                                 "achieved_gbs": round(L0.algo_bytes() / ldur / 1e9, 1),
+                                 "kernels": "qsched + qdecode_mma + xdecode_mma + combine"}}
 
     # ---- end to end through the public API with host buffers
     e2e = None
@@ -398,10 +404,10 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu:
         S = a.cpu_seqs
-        tps, sec = cpu_sample(layers, qs, c32, s32, S)
+        tps, sec = cpu_sample(layers, qs, c32, s32, S, reps=a.cpu_reps)
         cpu = {"value": round(tps, 2), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"{S} of the 64 sequences x 32,768 tokens, all 6 layers, oracle/kv800_oracle.c "
-                         f"(OpenMP over sequence x kv head), one pass of {sec:.2f} s"}
+               "sample": f"{S} of the {a.seqs} sequences x {a.ctx:,} tokens, all 6 layers, oracle/kv800_oracle.c "
+                         f"(OpenMP over sequence x kv head), median of {a.cpu_reps} passes of {sec:.2f} s"}
 
     if world > 1:
         dist.destroy_process_group()
@@ -423,13 +429,14 @@ def main():
 
 def reference_arm(a, rank, world, n_gpus):
     """The reference's CPU path for this step (the oracle port of torch_decode, all host threads) on a bounded sample:
-    S sequences of the 64 x 32K, 6-layer workload per step, K steps after W warm-ups."""
+    S = cores / 4 (at most 4) sequences of the 64 x 32K, 6-layer workload per step, so that every host thread has a
+    (sequence, kv head) item (about 0.2 s per step on 16 cores), exactly K steps after W warm-ups."""
     if rank != 0:
         return
     import torch
     from oracle import oracle as O
     O.lib()
-    S = 4
+    S = max(1, min(4, (os.cpu_count() or 4) // 4))   # the oracle runs (sequence x kv head) items in parallel
     # the workload built on the CPU side with the oracle's own quantizer (no GPU used by this arm)
     rs = np.random.RandomState(99)
     import inputs as I
@@ -468,9 +475,9 @@ def reference_arm(a, rank, world, n_gpus):
         for P, q in per_layer:
             O.decode(P, q, cs, sn)
 
-    for _ in range(min(a.warmup, 1)):
+    for _ in range(a.warmup):
         step()
-    steps = max(1, min(a.steps, 3))
+    steps = a.steps
     t0 = time.perf_counter()
     for _ in range(steps):
         step()
@@ -478,7 +485,7 @@ def reference_arm(a, rank, world, n_gpus):
     v = S / dt
     cores = os.cpu_count()
     line = {"metric": METRIC, "value": round(v, 2), "unit": "tok/s", "n_gpus": n_gpus, "steps": steps,
-            "warmup": min(a.warmup, 1), "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True,
+            "warmup": a.warmup, "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "u8+bf16 (fp32 math)", "data": "synthetic",
             "impl": "reference",
             "config": {"workload": "config 3: 64 seq x 32768 ctx per GPU, 4 quantized (127 sub-blocks + 256 exact) + "

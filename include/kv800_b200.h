@@ -217,6 +217,16 @@ KV800_API int kv800_decode_noalloc(const kv800_paged* P, const uint16_t* q, cons
                                    void* stream);
 
 /*
+ * kv800_decode_timed -- has no counterpart in the reference: kv800_decode with CUDA events around its phases, for
+ * benchmarks.  Blocks until the decode is done and writes ms[0] = the quantized partials (schedule + qdecode_mma),
+ * ms[1] = the exact partials (xdecode_mma), ms[2] = the combine, in milliseconds of device time.  A phase with no work
+ * reports the gap between its two events (about zero).
+ */
+KV800_API int kv800_decode_timed(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t,
+                                 const uint16_t* sin_t, int64_t npos, int64_t B, int64_t spb, uint16_t* out,
+                                 void* workspace, int64_t workspace_bytes, void* stream, float* ms);
+
+/*
  * The reference's three native decode ops (kv800::qdecode / xdecode / combine, csrc/kv800_sycl.sycl:554-561) with
  * the same argument meaning and partial layout: MO / LO (B, ns + 1, 16) f32, AO (B, ns + 1, 16, 128) f32; slots
  * [0, ns) are the quantized splits (V accumulated in the Hadamard domain), slot ns the sinks + exact tokens.

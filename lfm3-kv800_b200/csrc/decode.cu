@@ -267,9 +267,11 @@ static int check_tables(const uint16_t* cos_t, const uint16_t* sin_t, int64_t np
     return KV800_OK;
 }
 
-extern "C" int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t, const uint16_t* sin_t,
-                            int64_t npos, int64_t B, int64_t spb, uint16_t* out, void* workspace,
-                            int64_t workspace_bytes, void* stream) {
+// The decode of kv800_decode; ev (4 events or null) is recorded before the quantized partials, after them, after the
+// exact partials and after the combine.
+static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t, const uint16_t* sin_t,
+                       int64_t npos, int64_t B, int64_t spb, uint16_t* out, void* workspace, int64_t workspace_bytes,
+                       void* stream, cudaEvent_t* ev) {
     int rc = check_paged(P, "kv800_decode");
     if (rc) return rc;
     if (B < 0 || B > MAX_B) {
@@ -314,6 +316,7 @@ extern "C" int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint1
     float* ao = reinterpret_cast<float*>(ws + pl.ao_off);
     rc = cuda_status(cudaMemsetAsync(status, 0, sizeof(int), st), "kv800_decode status reset");
     if (rc) return rc;
+    if (ev) cudaEventRecord(ev[0], st);
     SlotMap sm{};
     sm.nx = NX_DEFAULT;
     if (pl.persistent) {
@@ -350,12 +353,44 @@ extern "C" int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint1
     }
     rc = xdecode_setup();
     if (rc) return rc;
+    if (ev) cudaEventRecord(ev[1], st);
     XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, sm.xbase, sm.xstride, NX_DEFAULT, SCALE, status};
     launch_xdecode(xa, dim3((unsigned)B, (unsigned)NX_DEFAULT), st);
     rc = cuda_status(cudaGetLastError(), "kv800_decode xdecode");
     if (rc) return rc;
+    if (ev) cudaEventRecord(ev[2], st);
     combine_kernel<<<(unsigned)B, 512, 0, st>>>(mo, lo, ao, sm, out);
-    return cuda_status(cudaGetLastError(), "kv800_decode combine");
+    rc = cuda_status(cudaGetLastError(), "kv800_decode combine");
+    if (ev) cudaEventRecord(ev[3], st);
+    return rc;
+}
+
+extern "C" int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t, const uint16_t* sin_t,
+                            int64_t npos, int64_t B, int64_t spb, uint16_t* out, void* workspace,
+                            int64_t workspace_bytes, void* stream) {
+    return decode_core(P, q, cos_t, sin_t, npos, B, spb, out, workspace, workspace_bytes, stream, nullptr);
+}
+
+extern "C" int kv800_decode_timed(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t,
+                                  const uint16_t* sin_t, int64_t npos, int64_t B, int64_t spb, uint16_t* out,
+                                  void* workspace, int64_t workspace_bytes, void* stream, float* ms) {
+    if (!ms) {
+        set_error("kv800_decode_timed: null ms");
+        return KV800_ERR_ARG;
+    }
+    cudaEvent_t ev[4];
+    for (int i = 0; i < 4; i++) {
+        const int rc = cuda_status(cudaEventCreate(&ev[i]), "kv800_decode_timed event");
+        if (rc) {
+            for (int j = 0; j < i; j++) cudaEventDestroy(ev[j]);
+            return rc;
+        }
+    }
+    int rc = decode_core(P, q, cos_t, sin_t, npos, B, spb, out, workspace, workspace_bytes, stream, ev);
+    if (!rc) rc = cuda_status(cudaEventSynchronize(ev[3]), "kv800_decode_timed sync");
+    for (int i = 0; i < 3 && !rc; i++) rc = cuda_status(cudaEventElapsedTime(&ms[i], ev[i], ev[i + 1]), "elapsed");
+    for (int i = 0; i < 4; i++) cudaEventDestroy(ev[i]);
+    return rc;
 }
 
 extern "C" int kv800_qdecode(const uint16_t* q, const uint8_t* qpool, int64_t qpool_bytes, const int64_t* boff,

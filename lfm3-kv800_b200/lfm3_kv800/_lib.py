@@ -5,7 +5,9 @@ import ctypes
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "_lib", "libkv800_b200.so")
+# LFM3KV_LIB names another build of the same library (e.g. an instrumented or experimental build); the default is the
+# in-tree build that build.py writes
+LIB_PATH = os.environ.get("LFM3KV_LIB") or os.path.join(HERE, "_lib", "libkv800_b200.so")
 
 OK, ERR_ARG, ERR_RANGE, ERR_CUDA, ERR_DEVICE = 0, 1, 2, 3, 4
 _p, _i64, _int, _f = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
@@ -44,6 +46,8 @@ SIGNATURES = {
     "kv800_write_exact": (_int, [_p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p]),
     "kv800_decode_workspace_size": (_i64, [_i64, _i64, _i64, _i64]),
     "kv800_decode": (_int, [ctypes.POINTER(Paged), _p, _p, _p, _i64, _i64, _i64, _p, _p, _i64, _p]),
+    "kv800_decode_timed": (_int, [ctypes.POINTER(Paged), _p, _p, _p, _i64, _i64, _i64, _p, _p, _i64, _p,
+                                  ctypes.POINTER(ctypes.c_float)]),
     "kv800_decode_noalloc": (_int, [ctypes.POINTER(Paged), _p, _p, _p, _i64, _i64, _i64, _p, _p]),
     "kv800_qdecode": (_int, [_p, _p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _f, _p,
                              _p]),

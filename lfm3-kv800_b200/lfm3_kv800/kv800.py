@@ -276,6 +276,19 @@ def decode(P, q, cos_t, sin_t, H=None, spb=None, target=None):
     whose keys need no rotation (native sliding layers); H: accepted for signature compatibility (the kernels
     apply the normalized 128-point Hadamard themselves).  spb: sub-blocks per split; target: the reference's split
     sizing knob (spb = ceil(nqmax * B * 4 / target)); both None = the library's choice for 148 SMs."""
+    return _decode(P, q, cos_t, sin_t, spb, target, None)
+
+
+def decode_timed(P, q, cos_t, sin_t, spb=None):
+    """decode() with CUDA-event timing of its phases (benchmarks; no counterpart in the reference).  Synchronizes.
+    -> (out, {"quantized_ms": schedule + qdecode_mma, "exact_ms": xdecode_mma, "combine_ms": combine})."""
+    ms = (ctypes.c_float * 3)()
+    out = _decode(P, q, cos_t, sin_t, spb, None, ms)
+    return out, {"quantized_ms": ms[0], "exact_ms": ms[1], "combine_ms": ms[2]}
+
+
+def _decode(P, q, cos_t, sin_t, spb, target, ms):
+    """decode() / decode_timed(); ms: a ctypes float[3] for the phase timings, or None."""
     _cuda(q, "decode")
     dt = q.device.type
     _LAST[0] = _resolve(dt)
@@ -306,8 +319,12 @@ def decode(P, q, cos_t, sin_t, H=None, spb=None, target=None):
     spb = int(spb or 0)
     ws_bytes = int(_lib.lib().kv800_decode_workspace_size(B, nqmax, s.win, spb))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-    _lib.call("kv800_decode", ctypes.byref(s), _ptr(q), _ptr(cs), _ptr(sn), npos, B, spb, _ptr(out),
-              _ptr(ws), ws_bytes, _stream(dev))
+    if ms is None:
+        _lib.call("kv800_decode", ctypes.byref(s), _ptr(q), _ptr(cs), _ptr(sn), npos, B, spb, _ptr(out),
+                  _ptr(ws), ws_bytes, _stream(dev))
+    else:
+        _lib.call("kv800_decode_timed", ctypes.byref(s), _ptr(q), _ptr(cs), _ptr(sn), npos, B, spb, _ptr(out),
+                  _ptr(ws), ws_bytes, _stream(dev), ms)
     _check_status(ws[:4].view(torch.int32), dev, "decode")
     del keep
     return out
