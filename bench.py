@@ -259,6 +259,134 @@ def flush_bench(kv800, torch, dev, reps=10):
             "fma_tflops": round(2 * 16.8e6 * 112 / t_pre / 1e12, 1)}
 
 
+def next_rows_bench(kv800, torch, dev, reps=10):
+    """The rows after the decode, each on its own seeded synthetic case:
+    vllm_step   one decode step of a quantized layer through vllm_step.KV800Attention.forward for 64 requests at
+                ~32K tokens with vLLM-shaped caches (exact blocks of 128 tokens, 262,144-B quant pages, shuffled
+                block tables; half of the requests cross the flush boundary this step, so the step flushes 32
+                sub-blocks), against kv800.decode alone on the same caches;
+    prefill_kv  the K / V a 32,768-token extend attends to: 127 dequantized sub-blocks + 256 exact rows + a 1-token
+                chunk, rotated, bf16 (output bytes / time);
+    train       fake_quant_k (as (8, 16, 256, 512) groups) / fake_quant_v on (8, 4096, 4, 128) fp32 activations
+                (bytes in + out / time);
+    sliding     a native sliding layer's decode (64 rows, window 256) without tables vs with identity tables."""
+    from lfm3_kv800 import train as T
+    from lfm3_kv800 import vllm_step as S
+    g = torch.Generator(device="cpu").manual_seed(11)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / reps
+
+    out = {}
+    # ---- vLLM step over vLLM-shaped caches
+    R, ebs = 64, 128
+    n_new = [32640 if r % 2 == 0 else 32641 for r in range(R)]   # 32,640 = 256 x 126 + 384: flushes sub-block 126
+    pages, qpages = -(-max(n_new) // ebs), -(-max(n_new) // S.QBLOCK)
+    live = 6                                             # exact blocks a request keeps (the 640-token window + slack)
+    nblk = R * live + 1
+    bt = torch.zeros(R, pages, dtype=torch.int32)
+    perm = torch.randperm(nblk - 1, generator=g) + 1
+    for r in range(R):
+        last = (n_new[r] - 1) // ebs
+        bt[r, last - live + 1:last + 1] = perm[r * live:(r + 1) * live].to(torch.int32)
+    qperm = torch.randperm(R * qpages, generator=g).view(R, qpages).to(torch.int32)
+    ev = (torch.randn(nblk, 4, ebs, 256, generator=g)).to(torch.bfloat16).to(dev)
+    npg = R * qpages
+    qraw = torch.zeros(npg * S.QPAGE, dtype=torch.uint8, device=dev)
+    pv = qraw.view(npg, S.QPAGE)
+    for p0 in range(0, npg, 64):                        # every sub-block slot holds real quantized data
+        p1 = min(npg, p0 + 64)
+        m = (p1 - p0) * 5
+        k = torch.randn(m, 256, 4, 128, device=dev).to(torch.bfloat16)
+        v = torch.randn(m, 256, 4, 128, device=dev).to(torch.bfloat16)
+        pv[p0:p1, :5 * SUB] = kv800.quantize_blocks(k, v).view(p1 - p0, 5 * SUB)
+    qv = torch.as_strided(qraw, (R * qpages, 2, S.QBLOCK, 4, S.QCONTENT),
+                          (S.QPAGE, S.QBLOCK * 4 * S.QCONTENT, 4 * S.QCONTENT, S.QCONTENT, 1))
+    sl = torch.tensor(n_new, dtype=torch.int32)
+    qsl = torch.arange(R + 1, dtype=torch.int32)
+    pos = sl.long() - 1
+    slot = (bt[torch.arange(R), (pos // ebs)].long() * ebs + pos % ebs)
+    q = torch.randn(R, 16, 128, generator=g).to(torch.bfloat16).to(dev)
+    k1 = torch.randn(R, 4, 128, generator=g).to(torch.bfloat16).to(dev)
+    v1 = torch.randn(R, 4, 128, generator=g).to(torch.bfloat16).to(dev)
+    attn = S.KV800Attention(6, 33000)
+    bt_d, slot_d, sl_d, qsl_d, pos_d, qbt_d = (t.to(dev) for t in (bt, slot, sl, qsl, pos, qperm))
+
+    def vstep():                                        # the metadata lives on the device, as vLLM keeps it
+        mx = S.build_meta(bt_d, slot_d, sl_d, qsl_d, sl, qsl, pos_d, R)
+        mq = S.build_meta(qbt_d, slot_d, sl_d, qsl_d, sl, qsl, pos_d, R)
+        return attn.forward(q, k1, v1, mx, ev, mq=mq, qv=qv)
+    t_step = timed(vstep)
+    # the step has no host sync, so it also runs as one CUDA graph: the graph replay is its device time without the
+    # Python / launch overhead of eager mode
+    t_graph = None
+    try:
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            vstep()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        with torch.cuda.graph(graph):
+            vstep()
+        t_graph = timed(graph.replay)
+        del graph
+    except Exception as ex:                             # report, do not fail the bench
+        t_graph = f"capture failed: {type(ex).__name__}: {str(ex)[:120]}"
+    mx = S.build_meta(bt_d, slot_d, sl_d, qsl_d, sl, qsl, pos_d, R)
+    c32, s32, _, _ = S.tables(dev, 33000)
+    qs0 = qv.stride(0)
+    nqmax = max(S.nq_of(n) for n in n_new)
+    tb = S.decode_tables(mx.seq_lens, R, mx.block_table, ev.stride(0), qbt_d, qs0, S.QBLOCK, nqmax)
+    P = kv800.Paged(qpool=qv, boff=tb["boff"], epool=ev, eoff=tb["eoff"], ebs=ebs, e_hs=ev.stride(1),
+                    e_ts=ev.stride(2), e_v=128, N=tb["N"], NQ=tb["NQ"], nqmax=nqmax, win=0)
+    t_dec = timed(lambda: kv800.decode(P, q, c32, s32))
+    out["vllm_step"] = {"requests": R, "flushed_subblocks": R // 2, "eager_step_us": round(t_step * 1e6, 1),
+                        "graph_step_us": round(t_graph * 1e6, 1) if isinstance(t_graph, float) else t_graph,
+                        "decode_only_us": round(t_dec * 1e6, 1),
+                        "launches": "write_slots, flush plan + flush, decode tables, 4 decode kernels"}
+    # ---- prefill / extend history assembly for one 32K request
+    r0 = 0
+    nq0 = S.nq_of(n_new[r0] - 1)
+    ch_k, ch_v = k1[:1], v1[:1]
+
+    def pk():
+        return S.prefill_kv(n_new[r0] - 1, n_new[r0], ch_k, ch_v, ev, mx.block_table[r0], qv=qv,
+                            qbt_row=qbt_d[r0], nqp=nq0, cos_t=c32, sin_t=s32)
+    t_pk = timed(pk)
+    rows = nq0 * 256 + (n_new[r0] - nq0 * 256)
+    out["prefill_kv"] = {"tokens": rows, "us": round(t_pk * 1e6, 1),
+                         "out_gbs": round(rows * 2048 / t_pk / 1e9, 1),
+                         "in_bytes": nq0 * SUB + (rows - nq0 * 256) * 2048}
+    # ---- training fake quant
+    x = torch.randn(8, 4096, 4, 128, device=dev)
+    xk = x.view(8, 16, 256, 512)                         # (B, groups of 256 tokens, 256, 4 heads x 128 channels)
+    t_k = timed(lambda: T.fake_quant_k(xk))
+    t_v = timed(lambda: T.fake_quant_v(x))
+    nbytes = x.numel() * 8
+    out["train_fake_quant"] = {"shape": [8, 4096, 4, 128], "k_us": round(t_k * 1e6, 1), "v_us": round(t_v * 1e6, 1),
+                               "k_gbs": round(nbytes / t_k / 1e9, 1), "v_gbs": round(nbytes / t_v / 1e9, 1)}
+    # ---- native sliding layer (window 256, no sinks): no tables vs identity tables
+    Ps = kv800.Paged(qpool=ev, boff=tb["eoff"], epool=ev, eoff=tb["eoff"], ebs=ebs, e_hs=ev.stride(1),
+                     e_ts=ev.stride(2), e_v=128, N=tb["N"], NQ=torch.zeros_like(tb["NQ"]), nqmax=0, win=WIN)
+    _, _, one, zero = S.tables(dev, 33000)
+    t_nt = timed(lambda: kv800.decode(Ps, q, None, None))
+    t_id = timed(lambda: kv800.decode(Ps, q, one, zero))
+    sb_bytes = R * WIN * 2048
+    out["sliding"] = {"rows": R, "window": WIN, "no_tables_us": round(t_nt * 1e6, 1),
+                      "identity_tables_us": round(t_id * 1e6, 1), "gbs_no_tables": round(sb_bytes / t_nt / 1e9, 1)}
+    return out
+
+
 # ---------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -271,6 +399,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-flush", action="store_true", help="skip the quantize / flush measurement")
+    ap.add_argument("--no-next", action="store_true", help="skip the vLLM-step / prefill / train / sliding measurement")
     ap.add_argument("--seqs", type=int, default=B_PER_GPU, help="sequences per GPU (profiling: smaller cases)")
     ap.add_argument("--ctx", type=int, default=N_CTX, help="context length (profiling: smaller cases)")
     a = ap.parse_args()
@@ -400,6 +529,9 @@ def main():
     flush = None
     if not a.no_flush:
         flush = flush_bench(kv800, torch, dev)
+    nxt = None
+    if not a.no_next and world == 1:
+        nxt = next_rows_bench(kv800, torch, dev)
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu:
@@ -423,7 +555,7 @@ def main():
                 "hbm_gbs_step": round(step_bytes * a.steps / t / 1e9, 1),
                 "hbm_frac_step": round(step_bytes * a.steps / t / 1e9 / peaks()[0], 4),
                 "bytes_per_step_per_gpu": step_bytes, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_launches": launches_per_step * a.steps, "clocks": clocks, "flush": flush}
+                "gpu_launches": launches_per_step * a.steps, "clocks": clocks, "flush": flush, "next_rows": nxt}
         print(json.dumps(line), flush=True)
 
 

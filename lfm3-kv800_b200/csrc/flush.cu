@@ -2,14 +2,14 @@
 // with the reference torch quantizer (lfm3_kv800/kv800.py:56-76), plus the exact-page scatter of new tokens
 // (kv800.py:423-428, vllm_attn.py:261-269).
 //
-// One launch covers M sub-blocks with grid (M, 1 + VSPLIT):
-//   blockIdx.y == 0        K part: 4 heads x 128 channels; lo / hi over the 256 tokens per channel, fp8 lo and
-//                          scale (hi - lo) / 3, 2-bit codes (IEEE divide, round half to even), planar bytes.
-//   blockIdx.y == 1..4     V part for 64 tokens: y = v @ H per head as the sequential fp32 FMA chain over i that the
+// One launch covers M sub-blocks with grid (M, VSPLIT + HEADS); the long V CTAs come first in launch order:
+//   blockIdx.y == 0..3     V part for 64 tokens: y = v @ H per head as the sequential fp32 FMA chain over i that the
 //                          reference's CPU BLAS computes (bit-exact requirement), lo / hi per (token, 2-head group),
 //                          1-bit codes, planar bytes.
+//   blockIdx.y == 4..7     K part of head y - 4: 128 channels; lo / hi over the 256 tokens per channel, fp8 lo and
+//                          scale (hi - lo) / 3, 2-bit codes (IEEE divide, round half to even), planar bytes.
 // The V part is the arithmetic bound of the kernel (128 FMA per output element, 16.8 M FMA per sub-block); the K part
-// streams 256 KB per sub-block twice (the second pass is served by L2).
+// streams 256 KB per sub-block twice (the second pass is served by L2), 32 tokens per thread per pass.
 #include <cstdarg>
 #include <cstdio>
 
@@ -237,17 +237,21 @@ __global__ void __launch_bounds__(256) flush_kernel(Src src) {
     uint8_t* out = src.dst(m);
     if (out == nullptr) return;
 
-    if (blockIdx.y == 0) {
-        // ---------------- K part. thread = (token half, head, j); channels j, j+32, j+64, j+96 of head h.
-        __shared__ float slo[2][HEADS][DIM], shi[2][HEADS][DIM];
-        const int half = tid >> 7, h = (tid >> 5) & 3, j = lane;
+    if (blockIdx.y >= VSPLIT) {
+        // ---------------- K part of head h = blockIdx.y - VSPLIT.  thread = (token group grp of 32 tokens, j):
+        // channels j, j + 32, j + 64, j + 96 of the head for tokens 32 grp .. 32 grp + 31; per-channel lo / hi over
+        // the 256 tokens through shared memory.
+        __shared__ float slo[8][DIM], shi[8][DIM];
+        const int h = blockIdx.y - VSPLIT, grp = warp, j = lane;
         float lo[4], hi[4];
 #pragma unroll
         for (int p = 0; p < 4; p++) {
             lo[p] = __int_as_float(0x7f800000);
             hi[p] = -__int_as_float(0x7f800000);
         }
-        for (int t = half * 128; t < half * 128 + 128; t++) {
+#pragma unroll 4
+        for (int i = 0; i < 32; i++) {
+            const int t = grp * 32 + i;
             const uint16_t *kr, *vr;
             float x[4] = {0.f, 0.f, 0.f, 0.f};
             if (src.rows(m, t, h, kr, vr)) {
@@ -262,25 +266,32 @@ __global__ void __launch_bounds__(256) flush_kernel(Src src) {
         }
 #pragma unroll
         for (int p = 0; p < 4; p++) {
-            slo[half][h][j + 32 * p] = lo[p];
-            shi[half][h][j + 32 * p] = hi[p];
+            slo[grp][j + 32 * p] = lo[p];
+            shi[grp][j + 32 * p] = hi[p];
         }
         __syncthreads();
         float lof[4], scf[4];
 #pragma unroll
         for (int p = 0; p < 4; p++) {
             const int c = j + 32 * p;
-            float l = fminf(slo[0][h][c], slo[1][h][c]), u = fmaxf(shi[0][h][c], shi[1][h][c]);
+            float l = slo[0][c], u = shi[0][c];
+#pragma unroll
+            for (int q = 1; q < 8; q++) {
+                l = fminf(l, slo[q][c]);
+                u = fmaxf(u, shi[q][c]);
+            }
             uint32_t lo8 = f8enc(l);
             uint32_t sc8 = f8enc(clamp_min_1e8(__fdiv_rn(u - l, 3.0f)));
             lof[p] = f8dec(lo8);
             scf[p] = clamp_min_1e8(f8dec(sc8));
-            if (half == 0) {
+            if (grp == 0) {
                 out[KLO_O + h * DIM + c] = (uint8_t)lo8;
                 out[KSC_O + h * DIM + c] = (uint8_t)sc8;
             }
         }
-        for (int t = half * 128; t < half * 128 + 128; t++) {
+#pragma unroll 4
+        for (int i = 0; i < 32; i++) {
+            const int t = grp * 32 + i;
             const uint16_t *kr, *vr;
             float x[4] = {0.f, 0.f, 0.f, 0.f};
             if (src.rows(m, t, h, kr, vr)) {
@@ -299,7 +310,7 @@ __global__ void __launch_bounds__(256) flush_kernel(Src src) {
     __shared__ float vbuf[8][HEADS * DIM];
     float C[32];
     hadamard_signs(lane, C);
-    const int t0 = (blockIdx.y - 1) * VTOK;
+    const int t0 = blockIdx.y * VTOK;
     for (int tt = warp; tt < VTOK; tt += 8) {
         const int t = t0 + tt;
         // stage the 4 V rows (512 values) of token t as fp32: lane loads 16 values of head lane / 8
@@ -522,7 +533,7 @@ extern "C" int kv800_quantize_blocks(const uint16_t* k, const uint16_t* v, int64
         return KV800_ERR_RANGE;
     }
     ContigSrc s{k, v, out};
-    flush_kernel<ContigSrc><<<dim3((unsigned)M, 1 + VSPLIT), 256, 0, as_stream(stream)>>>(s);
+    flush_kernel<ContigSrc><<<dim3((unsigned)M, HEADS + VSPLIT), 256, 0, as_stream(stream)>>>(s);
     return cuda_status(cudaGetLastError(), "kv800_quantize_blocks launch");
 }
 
@@ -545,7 +556,7 @@ extern "C" int kv800_flush(const uint16_t* epool, int64_t epool_elems, const int
     }
     PagedSrc s{epool, epool_elems, eoff, eoff_stride, ebs, e_hs, e_ts, e_v, qpool, qpool_bytes,
                boff, boff_stride, seq, blk, nseq, status};
-    flush_kernel<PagedSrc><<<dim3((unsigned)M, 1 + VSPLIT), 256, 0, as_stream(stream)>>>(s);
+    flush_kernel<PagedSrc><<<dim3((unsigned)M, HEADS + VSPLIT), 256, 0, as_stream(stream)>>>(s);
     return cuda_status(cudaGetLastError(), "kv800_flush launch");
 }
 
@@ -678,6 +689,6 @@ extern "C" int kv800_flush_step(const uint16_t* ecache, int64_t ecache_elems, in
     if (rc) return rc;
     VllmSrc src{ecache, ecache_elems, s0, s1, s2, ebs, block_table, bt_stride, qcache, qcache_bytes, qs0, bsq,
                 qblock_table, qbt_stride, pairs, count, R, status};
-    flush_kernel<VllmSrc><<<dim3((unsigned)max_pairs, 1 + VSPLIT), 256, 0, st>>>(src);
+    flush_kernel<VllmSrc><<<dim3((unsigned)max_pairs, HEADS + VSPLIT), 256, 0, st>>>(src);
     return cuda_status(cudaGetLastError(), "kv800_flush_step flush");
 }
