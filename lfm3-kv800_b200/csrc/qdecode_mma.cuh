@@ -119,20 +119,17 @@ __device__ __forceinline__ void reg_dims(int tig, int i, int& d0, int& d1) {
     }
 }
 
-// Register layout of one token's QK A operand for thread tig (bytes J = 8 tig .. 8 tig + 7 of the kc row):
-//   R[u], u < 8      (kr0_j, kr2_j), j = 8 tig + u              (RoPE dims j and j + 64)
-//   R[8 + pi]        (k1_j, k1_{j+2}), j = 8 tig + {0,1,4,5}[pi] (NoPE dims 32 + j, 32 + j + 2)
-//   R[12 + pi]       (k3_j, k3_{j+2})                            (NoPE dims 96 + j, 96 + j + 2)
-// K-step ks uses R[2 ks] for columns (2 tig, 2 tig + 1) and R[2 ks + 1] for columns (2 tig + 8, 2 tig + 9).
+// Register layout of one token's QK A operand for thread tig (bytes J = 8 tig .. 8 tig + 7 of the kc row), in two
+// halves so that only one is live at a time:
+//   rotated  R[u], u < 8   (kr0_j, kr2_j), j = 8 tig + u              (RoPE dims j and j + 64)      K-steps 0..3
+//   NoPE     R[pi]         (k1_j, k1_{j+2}), j = 8 tig + {0,1,4,5}[pi] (dims 32 + j, 32 + j + 2)     K-steps 4..7
+//            R[4 + pi]     (k3_j, k3_{j+2})                            (dims 96 + j, 96 + j + 2)
+// K-step ks of a half uses R[2 ks] for columns (2 tig, 2 tig + 1) and R[2 ks + 1] for columns (2 tig + 8, 2 tig + 9).
 //
 // Per-plane code encodings (bf16, code c at mantissa bits of the plane): x = 4 + c * 2^(2p - 5) for planes 0..2 and
 // plane 3 shifted down by 4 bits (encoded like plane 1), so (x - 4) * (sc * 2^(5 - 2p)) = c * sc exactly and
-// fma(x - 4, A, lo) = bf16(c sc + lo) with one rounding.
-struct DequantConsts {
-    uint32_t A[4][4];    // [plane][pair]: bf16x2 of sc_j * 2^(5 - 2p') for the pair (j, j + 2)
-    uint32_t L[4][4];    // [plane][pair]: bf16x2 of lo_j, lo_{j+2}
-};
-
+// fma(x - 4, A, lo) = bf16(c sc + lo) with one rounding.  The per-sub-block constants (A, L) of a plane for the
+// thread's 4 pairs are two 16-byte words in shared memory: (A0, L0, A1, L1), (A2, L2, A3, L3).
 
 // RoPE of two key pairs with the reference's roundings, on packed bf16 operands (mixed-precision fma.rn.f32.bf16:
 // bf16 x bf16 products are exact in fp32, so t = fma(k2, sn, 0) is k2 sn and fma(k0, cs, -t) is the reference's
@@ -168,32 +165,42 @@ __device__ __forceinline__ void rope_pairs(uint32_t k0, uint32_t k2, uint32_t ca
     }
 }
 
-__device__ __forceinline__ void token_regs(uint32_t w0, uint32_t w1, const uint4& cw, const uint4& sw,
-                                           const DequantConsts& K, uint32_t (&R)[16], uint32_t BASE) {
-    // BASE = bf16x2 (4.0, 4.0) from the kernel arguments
-    // pair words: byte pair (j, j + 2) at bits 0-7 / 16-23
+// The rotated half of one token's A registers: planes 0 and 2 dequantized (KC = their constant words) and rotated.
+// BASE = bf16x2 (4, 4) from the kernel arguments; w0 / w1 = the thread's 8 code bytes (pair words: byte pair (j,
+// j + 2) at bits 0-7 / 16-23).
+__device__ __forceinline__ void token_rope(uint32_t w0, uint32_t w1, const uint4& cw, const uint4& sw,
+                                           const uint4 (&KC)[4], uint32_t (&R)[8], uint32_t BASE) {
     const uint32_t pw[4] = {w0, w0 >> 8, w1, w1 >> 8};
     const uint32_t cwv[4] = {cw.x, cw.y, cw.z, cw.w};   // cos of j = 8tig + {0,1}, {2,3}, {4,5}, {6,7}
     const uint32_t swv[4] = {sw.x, sw.y, sw.z, sw.w};
+    // KC[0..1]: plane 0 (A, L) x 4 pairs, KC[2..3]: plane 2
+    const uint32_t A0[4] = {KC[0].x, KC[0].z, KC[1].x, KC[1].z}, L0[4] = {KC[0].y, KC[0].w, KC[1].y, KC[1].w};
+    const uint32_t A2[4] = {KC[2].x, KC[2].z, KC[3].x, KC[3].z}, L2[4] = {KC[2].y, KC[2].w, KC[3].y, KC[3].w};
 #pragma unroll
     for (int pi = 0; pi < 4; pi++) {
         const uint32_t P = pw[pi];
-        // NoPE planes 1 and 3 -> A registers directly
-        const uint32_t x1 = lop3_and_or(P, 0x000c000cu, BASE);
-        R[8 + pi] = hfma2_bf16(hsub2_bf16(x1, BASE), K.A[1][pi], K.L[1][pi]);
-        const uint32_t x3 = lop3_and_or(P >> 4, 0x000c000cu, BASE);
-        R[12 + pi] = hfma2_bf16(hsub2_bf16(x3, BASE), K.A[3][pi], K.L[3][pi]);
-        // RoPE planes 0 and 2: bf16 keys, then rotation in fp32 and the second rounding
-        const uint32_t x0 = lop3_and_or(P, 0x00030003u, BASE);
-        const uint32_t k0 = hfma2_bf16(hsub2_bf16(x0, BASE), K.A[0][pi], K.L[0][pi]);
-        const uint32_t x2 = lop3_and_or(P, 0x00300030u, BASE);
-        const uint32_t k2 = hfma2_bf16(hsub2_bf16(x2, BASE), K.A[2][pi], K.L[2][pi]);
+        const uint32_t k0 = hfma2_bf16(hsub2_bf16(lop3_and_or(P, 0x00030003u, BASE), BASE), A0[pi], L0[pi]);
+        const uint32_t k2 = hfma2_bf16(hsub2_bf16(lop3_and_or(P, 0x00300030u, BASE), BASE), A2[pi], L2[pi]);
         // the pair is (j, j + 2) with j = 8 tig + {0, 1, 4, 5}[pi]: cos / sin words {0,1} (pi < 2) or {2,3},
         // low halves for even j, high halves for odd j
         const int wi = (pi >> 1) * 2;
         const bool odd = (pi & 1) != 0;
         const int ua = (pi & 1) | ((pi & 2) << 1);   // u of byte j = 8 tig + u
         rope_pairs(k0, k2, cwv[wi], cwv[wi + 1], swv[wi], swv[wi + 1], odd, R[ua], R[ua + 2]);
+    }
+}
+
+// The NoPE half: planes 1 and 3 (KC = their constant words) dequantized straight into A registers.
+__device__ __forceinline__ void token_nope(uint32_t w0, uint32_t w1, const uint4 (&KC)[4], uint32_t (&R)[8],
+                                           uint32_t BASE) {
+    const uint32_t pw[4] = {w0, w0 >> 8, w1, w1 >> 8};
+    const uint32_t A1[4] = {KC[0].x, KC[0].z, KC[1].x, KC[1].z}, L1[4] = {KC[0].y, KC[0].w, KC[1].y, KC[1].w};
+    const uint32_t A3[4] = {KC[2].x, KC[2].z, KC[3].x, KC[3].z}, L3[4] = {KC[2].y, KC[2].w, KC[3].y, KC[3].w};
+#pragma unroll
+    for (int pi = 0; pi < 4; pi++) {
+        const uint32_t P = pw[pi];
+        R[pi] = hfma2_bf16(hsub2_bf16(lop3_and_or(P, 0x000c000cu, BASE), BASE), A1[pi], L1[pi]);
+        R[4 + pi] = hfma2_bf16(hsub2_bf16(lop3_and_or(P >> 4, 0x000c000cu, BASE), BASE), A3[pi], L3[pi]);
     }
 }
 
@@ -471,6 +478,12 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
             // read the same rows, served by L1)
             const uint16_t* crow0 = a.cos_t + (pos0 + g) * 32 + 8 * tig;
             const uint16_t* srow0 = a.sin_t + (pos0 + g) * 32 + 8 * tig;
+            // table rows of the next tile, loaded right after the current tile's key registers are built so the
+            // load latency overlaps the QK MMAs (and the softmax / PV at the chunk's end)
+            uint4 nca = *reinterpret_cast<const uint4*>(crow0);
+            uint4 nsa = *reinterpret_cast<const uint4*>(srow0);
+            uint4 ncb = *reinterpret_cast<const uint4*>(crow0 + 8 * 32);
+            uint4 nsb = *reinterpret_cast<const uint4*>(srow0 + 8 * 32);
 #pragma unroll 1
             for (int c0 = 0; c0 < QM_HALF; c0 += 32) {
                 float sc[2][4];
@@ -478,38 +491,42 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
 #pragma unroll
                 for (int mt = 0; mt < 2; mt++) {
                     const int t0 = c0 + 16 * mt;
-                    uint32_t R0[16], R1[16];
+                    float sx[4] = {0.f, 0.f, 0.f, 0.f};
                     {
                         const uint8_t* kt = raw + t0 * 128;
                         const uint2 kwa = *reinterpret_cast<const uint2*>(kt + koff_a);
                         const uint2 kwb = *reinterpret_cast<const uint2*>(kt + koff_b);
-                        const uint16_t* crow = crow0 + t0 * 32;
-                        const uint16_t* srow = srow0 + t0 * 32;
-                        const uint4 ca = *reinterpret_cast<const uint4*>(crow);
-                        const uint4 sa = *reinterpret_cast<const uint4*>(srow);
-                        const uint4 cb = *reinterpret_cast<const uint4*>(crow + 8 * 32);
-                        const uint4 sbw = *reinterpret_cast<const uint4*>(srow + 8 * 32);
-                        DequantConsts K;
-#pragma unroll
-                        for (int p = 0; p < 4; p++) {
-                            const uint4 w0 = cstp[((h * 4 + p) * 4 + tig) * 2];
-                            const uint4 w1 = cstp[((h * 4 + p) * 4 + tig) * 2 + 1];
-                            K.A[p][0] = w0.x; K.L[p][0] = w0.y; K.A[p][1] = w0.z; K.L[p][1] = w0.w;
-                            K.A[p][2] = w1.x; K.L[p][2] = w1.y; K.A[p][3] = w1.z; K.L[p][3] = w1.w;
+                        const uint4 ca = nca, sa = nsa, cb = ncb, sbw = nsb;
+                        const uint4* cp = cstp + (h * 4 * 4 + tig) * 2;   // [plane p] at + p * 8
+                        uint32_t Ra[8], Rb[8];
+                        {
+                            const uint4 KC[4] = {cp[0], cp[1], cp[16], cp[17]};   // planes 0, 2
+                            token_rope(kwa.x, kwa.y, ca, sa, KC, Ra, a.kbase);
+                            token_rope(kwb.x, kwb.y, cb, sbw, KC, Rb, a.kbase);
                         }
-                        token_regs(kwa.x, kwa.y, ca, sa, K, R0, a.kbase);
-                        token_regs(kwb.x, kwb.y, cb, sbw, K, R1, a.kbase);
-                    }
-                    // two accumulator chains (even / odd K-steps) halve the dependent-MMA latency
-                    float sx[4] = {0.f, 0.f, 0.f, 0.f}, sy[4] = {0.f, 0.f, 0.f, 0.f};
+                        if (t0 + 16 < QM_HALF) {
+                            const uint16_t* crow = crow0 + (t0 + 16) * 32;
+                            const uint16_t* srow = srow0 + (t0 + 16) * 32;
+                            nca = *reinterpret_cast<const uint4*>(crow);
+                            nsa = *reinterpret_cast<const uint4*>(srow);
+                            ncb = *reinterpret_cast<const uint4*>(crow + 8 * 32);
+                            nsb = *reinterpret_cast<const uint4*>(srow + 8 * 32);
+                        }
 #pragma unroll
-                    for (int ks = 0; ks < 8; ks += 2) {
-                        mma_bf16(sx, R0[2 * ks], R1[2 * ks], R0[2 * ks + 1], R1[2 * ks + 1], bq[ks][0], bq[ks][1]);
-                        mma_bf16(sy, R0[2 * ks + 2], R1[2 * ks + 2], R0[2 * ks + 3], R1[2 * ks + 3], bq[ks + 1][0],
-                                 bq[ks + 1][1]);
+                        for (int ks = 0; ks < 4; ks++)
+                            mma_bf16(sx, Ra[2 * ks], Rb[2 * ks], Ra[2 * ks + 1], Rb[2 * ks + 1], bq[ks][0], bq[ks][1]);
+                        {
+                            const uint4 KC[4] = {cp[8], cp[9], cp[24], cp[25]};   // planes 1, 3
+                            token_nope(kwa.x, kwa.y, KC, Ra, a.kbase);
+                            token_nope(kwb.x, kwb.y, KC, Rb, a.kbase);
+                        }
+#pragma unroll
+                        for (int ks = 4; ks < 8; ks++)
+                            mma_bf16(sx, Ra[2 * (ks - 4)], Rb[2 * (ks - 4)], Ra[2 * (ks - 4) + 1], Rb[2 * (ks - 4) + 1],
+                                     bq[ks][0], bq[ks][1]);
                     }
 #pragma unroll
-                    for (int e = 0; e < 4; e++) sc[mt][e] = sx[e] + sy[e];
+                    for (int e = 0; e < 4; e++) sc[mt][e] = sx[e];
                     const float2 xa = vslh[2 * t0 + vsl_a], xb = vslh[2 * t0 + vsl_b];
                     vlv[mt][0] = xa.x; vsv[mt][0] = xa.y;
                     vlv[mt][1] = xb.x; vsv[mt][1] = xb.y;
