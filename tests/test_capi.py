@@ -60,6 +60,8 @@ def test_host_argument_checks():
     P = _lib.Paged()
     assert L.kv800_decode(ctypes.byref(P), None, None, None, 1, 1, 0, None, None, 0, None) == _lib.ERR_ARG
     assert L.kv800_check_status(None, None, None) == _lib.ERR_ARG
+    assert L.kv800_decode_timed(None, None, None, None, 1, 1, 0, None, None, 0, None, None) == _lib.ERR_ARG
+    assert L.kv800_decode_timed(ctypes.byref(P), None, None, None, 1, 1, 0, None, None, 0, None, None) == _lib.ERR_ARG
 
 
 def test_step_entry_argument_checks():

@@ -69,3 +69,19 @@ def test_split_sizes_agree(kv800, tables, spb):
     """Every split size gives the reference's answer (split-K + combine is exact up to fp32 rounding)."""
     o, _, _, _ = run_case(kv800, tables, 0, 5000, spb=spb)
     assert_parity(o, DG["w0_n5000_out"], f"spb={spb}")
+
+
+@pytest.mark.parametrize("win,n", [(0, 1500), (256, 700)])
+def test_decode_timed_matches_decode(kv800, tables, win, n):
+    """kv800.decode_timed (the phase-timed entry the bench uses for its roofline) returns decode()'s exact output and
+    positive phase times (the exact phase always runs; the quantized phase only for quantized layers)."""
+    K, V, q = I.parity_inputs(win, n)
+    st = kv800.PagedStore(2, n + 8, DEV, window=win)
+    st.append(tb(K, DEV), tb(V, DEV))
+    c32, s32 = tables
+    ref = nb(kv800.decode(st.paged(), tb(q, DEV), c32, s32, st.H))
+    out, ms = kv800.decode_timed(st.paged(), tb(q, DEV), c32, s32)
+    assert np.array_equal(nb(out), ref)
+    assert ms["exact_ms"] > 0 and ms["combine_ms"] > 0 and ms["quantized_ms"] >= 0
+    if win == 0:
+        assert ms["quantized_ms"] > 0
