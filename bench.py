@@ -12,7 +12,8 @@ through the public API with the step's inputs (6 x q, the current token's K / V)
 current token written into its exact page, and the 6 outputs read back, all inside the timed region.  `roofline` =
 the quantized-split kernel (the dominant one) timed alone with CUDA events: algorithmic bytes (51,200 per sub-block)
 / duration against the measured HBM copy bandwidth.  `cpu_baseline` = the CPU oracle (a C port of the reference's
-torch decode, OpenMP over (sequence, kv head)) on 8 of the sequences, all 6 layers, on this host's cores.
+torch decode, OpenMP over (sequence, kv head)) on the 64 sequences, all 6 layers, on this host's cores.
+--workload ragged: BASELINE config 4 instead (2,048 ragged rows sharded over the ranks, strong scaling).
 
 --impl reference: the reference's CPU path for this step (the oracle port, all host threads) on a bounded sample of
 the same workload, printed as the reference arm's line; on N > 1 ranks only rank 0 runs it."""
@@ -116,6 +117,107 @@ def build_workload(kv800, torch, dev, rank, B=B_PER_GPU, n=N_CTX):
     s32 = torch.from_numpy(sn.view(np.int16)).view(torch.bfloat16).to(dev)
     qs = [torch.randn(B, 16, 128, device=dev).to(torch.bfloat16) for _ in layers]
     return layers, qs, c32, s32
+
+
+# ---------------------------------------------------------------- config 4: ragged rows in a big pool
+RAGGED_ROWS, RAGGED_LO, RAGGED_HI = 2048, 1024, 32768
+
+
+class RaggedLayer:
+    """One layer's 800h cache for rows of different lengths: sub-blocks at distinct random slots
+    of a shared pool (a view into a buffer of --pool-gb), exact pages at random slots of the layer's page pool.
+    Sub-block contents come from a pool of `uniq` distinct quantized sub-blocks (the decode's cost does not depend on
+    the values)."""
+
+    def __init__(self, kv800, torch, dev, lengths, win, gen, pool, slots, uniq):
+        self.win, self.B = win, len(lengths)
+        N = torch.tensor(lengths, dtype=torch.int64)
+        nq = torch.zeros_like(N) if win else torch.clamp(N - 128, min=0) // 256
+        lo = torch.clamp(N - win, min=0) if win else nq * 256
+        self.nqmax = int(nq.max())
+        self.lengths, self.nq_rows = lengths, nq.tolist()
+        self.exact_rows = (N - lo).tolist()
+        # exact pages: rows' pages [lo // EBS, (n - 1) // EBS] at random slots
+        first, last = lo // EBS, (N - 1) // EBS
+        cnt = (last - first + 1).clamp(min=0)
+        npages = int(cnt.sum())
+        perm = torch.randperm(npages + 3, generator=gen)[:npages]
+        npg_row = int(N.max()) // EBS + 1
+        self.eoff = torch.zeros(self.B, npg_row, dtype=torch.int64)
+        o = 0
+        for b in range(self.B):
+            c = int(cnt[b])
+            self.eoff[b, int(first[b]):int(first[b]) + c] = perm[o:o + c] * (4 * EBS * 256)
+            o += c
+        self.eoff = self.eoff.to(dev)
+        self.epool = torch.randn(npages + 3, 4, EBS, 256, device=dev).to(torch.bfloat16)
+        if not win:
+            self.qpool = pool
+            self.boff = torch.zeros(self.B, max(1, self.nqmax), dtype=torch.int64)
+            o = 0
+            for b in range(self.B):
+                k = int(nq[b])
+                self.boff[b, :k] = slots[o:o + k] * SUB
+                o += k
+            self.boff = self.boff.to(dev)
+            pick = torch.randint(0, uniq.shape[0], (o,), generator=gen).to(dev)
+            pool.view(-1, SUB)[slots[:o].to(dev)] = uniq[pick]
+            self.used = o
+        else:
+            self.qpool = torch.zeros(1, SUB, dtype=torch.uint8, device=dev)
+            self.boff = torch.zeros(self.B, 1, dtype=torch.int64, device=dev)
+            self.used = 0
+        if win:
+            self.sk = torch.randn(self.B, NSINK, 4, 128, device=dev).to(torch.bfloat16)
+            self.sv = torch.randn(self.B, NSINK, 4, 128, device=dev).to(torch.bfloat16)
+            self.skoff = (torch.arange(self.B, dtype=torch.int64) * NSINK * 512).to(dev)
+        else:
+            self.sk = self.sv = self.skoff = None
+        self.N = N.to(torch.int32).to(dev)
+        self.NQ = nq.to(torch.int32).to(dev)
+        self.P = kv800.Paged(qpool=self.qpool, boff=self.boff, epool=self.epool, eoff=self.eoff, ebs=EBS,
+                             e_hs=EBS * 256, e_ts=256, e_v=128, sk=self.sk, sv=self.sv, skoff=self.skoff,
+                             svoff=self.skoff, N=self.N, NQ=self.NQ, nqmax=self.nqmax, win=win)
+
+    def algo_bytes(self):
+        return sum(q * 256 * 200 + (e + (NSINK if self.win else 0)) * 2048
+                   for q, e in zip(self.nq_rows, self.exact_rows))
+
+
+def build_ragged(kv800, torch, dev, rank, world, pool_gb):
+    """Config 4: 2,048 rows with lengths ~ U[1024, 32768] (seeded, the same on every rank), sharded over the ranks by
+    longest-processing-time on their read bytes; this rank's rows in 4 quantized + 2 window layers.  The quantized
+    layers' sub-blocks are scattered over one pool of pool_gb GB."""
+    from lfm3_kv800 import dp
+    rs = np.random.RandomState(2048)
+    lengths_all = rs.randint(RAGGED_LO, RAGGED_HI + 1, RAGGED_ROWS).tolist()
+    rows = dp.shard_rows(lengths_all, world, rank)
+    lengths = [lengths_all[i] for i in rows]
+    gen = torch.Generator().manual_seed(4321 + rank)
+    nsub = sum(max(0, n - 128) // 256 for n in lengths) * QUANT_LAYERS
+    # exact pages of 6 layers (<= 8 pages of 32 KB x 4 heads per row) and their fp32 staging, then the pool in what is
+    # left of the GPU's free memory minus 8 GB
+    exact_bytes = 6 * len(lengths) * 8 * 4 * EBS * 256 * 2 * 3
+    free = torch.cuda.mem_get_info(dev)[0]
+    pool_bytes = min(int(pool_gb * 1e9), free - exact_bytes - int(8e9)) // SUB * SUB
+    pool_bytes = max(pool_bytes, (nsub + 16) * SUB)
+    pool = torch.empty(pool_bytes, dtype=torch.uint8, device=dev)
+    slots = torch.randperm(pool_bytes // SUB, generator=gen)[:nsub]
+    k = torch.randn(256, 256, 4, 128, device=dev).to(torch.bfloat16)
+    v = torch.randn(256, 256, 4, 128, device=dev).to(torch.bfloat16)
+    uniq = kv800.quantize_blocks(k, v)
+    layers, o = [], 0
+    for li in range(QUANT_LAYERS + WINDOW_LAYERS):
+        win = 0 if li < QUANT_LAYERS else WIN
+        L = RaggedLayer(kv800, torch, dev, lengths, win, gen, pool, slots[o:], uniq)
+        o += L.used
+        layers.append(L)
+    qs = [torch.randn(len(lengths), 16, 128, device=dev).to(torch.bfloat16) for _ in layers]
+    import inputs as I
+    cs, sn = I.rope_tables(RAGGED_HI + 64)
+    c32 = torch.from_numpy(cs.view(np.int16)).view(torch.bfloat16).to(dev)
+    s32 = torch.from_numpy(sn.view(np.int16)).view(torch.bfloat16).to(dev)
+    return layers, qs, c32, s32, rows, pool_bytes
 
 
 # ---------------------------------------------------------------- clocks sampled during the timed region
@@ -402,6 +504,10 @@ def main():
     ap.add_argument("--no-next", action="store_true", help="skip the vLLM-step / prefill / train / sliding measurement")
     ap.add_argument("--seqs", type=int, default=B_PER_GPU, help="sequences per GPU (profiling: smaller cases)")
     ap.add_argument("--ctx", type=int, default=N_CTX, help="context length (profiling: smaller cases)")
+    ap.add_argument("--workload", default="config3", choices=("config3", "ragged"),
+                    help="config3 (the metric's workload) or ragged (BASELINE config 4: 2,048 rows of U[1K, 32K] "
+                         "tokens sharded over the ranks, strong scaling)")
+    ap.add_argument("--pool-gb", type=float, default=150.0, help="ragged: the sub-block pool per GPU (GB)")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
 
@@ -422,6 +528,8 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
+    if a.workload == "ragged":
+        return ragged_main(a, kv800, torch, dist, dev, rank, world, local, n_gpus)
     layers, qs, c32, s32 = build_workload(kv800, torch, dev, rank, B=a.seqs, n=a.ctx)
     torch.cuda.synchronize()
     step_bytes = sum(L.algo_bytes() for L in layers)
@@ -556,6 +664,74 @@ def main():
                 "hbm_frac_step": round(step_bytes * a.steps / t / 1e9 / peaks()[0], 4),
                 "bytes_per_step_per_gpu": step_bytes, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": launches_per_step * a.steps, "clocks": clocks, "flush": flush, "next_rows": nxt}
+        print(json.dumps(line), flush=True)
+
+
+def ragged_main(a, kv800, torch, dist, dev, rank, world, local, n_gpus):
+    """Config 4: every rank decodes its LPT share of the 2,048 ragged rows through all 6 layers per step; value =
+    2,048 x steps / max-over-ranks device time (strong scaling: the total work is fixed)."""
+    layers, qs, c32, s32, rows, pool_bytes = build_ragged(kv800, torch, dev, rank, world, a.pool_gb)
+    torch.cuda.synchronize()
+    step_bytes = sum(L.algo_bytes() for L in layers)
+
+    def step():
+        return [kv800.decode(L.P, q, c32, s32) for L, q in zip(layers, qs)]
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        torch.cuda.synchronize()
+        ev0.record()
+        for _ in range(a.steps):
+            step()
+        ev1.record()
+        torch.cuda.synchronize()
+    t = ev0.elapsed_time(ev1) / 1e3
+    tmax = t
+    bytes_all = step_bytes
+    if world > 1:
+        tt = torch.tensor([t], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        tmax = float(tt.item())
+        bb = torch.tensor([float(step_bytes)], device=dev, dtype=torch.float64)
+        dist.all_reduce(bb)
+        bytes_all = float(bb.item())
+        dist.barrier()
+    # dominant kernel on this rank: the quantized phase of layer 0 (L2 flushed)
+    L0, q0 = layers[0], qs[0]
+    flushbuf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    kt = []
+    for _ in range(10):
+        flushbuf.fill_(1)
+        _, ms = kv800.decode_timed(L0.P, q0, c32, s32)
+        kt.append(ms["quantized_ms"] / 1e3)
+    kdur = statistics.median(kt)
+    kbytes = sum(L0.nq_rows) * SUB
+    hbm, peak_kind = peaks()
+    clocks = clk.summary()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(RAGGED_ROWS * a.steps / tmax, 1), "unit": "tok/s", "n_gpus": n_gpus,
+                "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(tmax / a.steps * 1e3, 4),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8+bf16 (fp32 math)",
+                "data": "synthetic",
+                "config": {"workload": f"config 4: {RAGGED_ROWS} rows, lengths U[{RAGGED_LO}, {RAGGED_HI}] (seed "
+                                       f"2048), LPT-sharded over {n_gpus} GPU(s), 4 quantized + 2 window layers, "
+                                       f"sub-blocks scattered over a {pool_bytes / 1e9:.0f} GB pool per GPU",
+                           "rows_rank0": len(rows), "parallelism": f"dp{n_gpus} (LPT row sharding, no collective)"},
+                "hbm_gbs_step": round(bytes_all * a.steps / tmax / 1e9, 1),
+                "bytes_per_step_all_gpus": int(bytes_all),
+                "roofline": {"bound": "hbm", "achieved": round(kbytes / kdur / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                             "frac": round(kbytes / kdur / 1e9 / hbm, 4), "traffic": None, "peak_source": peak_kind,
+                             "kernel": "qdecode_mma (+ its 1-CTA schedule scan), rank 0, layer 0",
+                             "bytes_per_launch": kbytes, "launch_us": round(kdur * 1e6, 1)},
+                "cpu_baseline": None, "e2e": None,
+                "gpu_launches": sum(4 if L.nqmax else 2 for L in layers) * a.steps, "clocks": clocks}
         print(json.dumps(line), flush=True)
 
 
