@@ -534,26 +534,28 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
                 // ---- online softmax over the 32 tokens for this thread's rows r = 2 tig, 2 tig + 1
                 // lazy rescale: the reference point m moves only when a score exceeds it by more than 2^6, so p <= 64
                 // and fp16(p * vs) <= 64 * 448 stays finite; the partial (m, l, acc) is exact for any m
-                float alpha[2] = {1.f, 1.f};
-                bool moved = false;
+                // the row maxima are reduced across the 8 lanes of a row only when some score of the warp passes its
+                // row's reference point by more than 2^6 (rare after the first chunk)
+                float lmx[2];
+                bool need = false;
 #pragma unroll
                 for (int rr = 0; rr < 2; rr++) {
-                    float mx = fmaxf(fmaxf(sc[0][rr], sc[0][rr + 2]), fmaxf(sc[1][rr], sc[1][rr + 2])) * a.scale;
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                    if (mx > m[rr] + 6.0f) {
-                        alpha[rr] = fast_exp2(m[rr] - mx);
-                        m[rr] = mx;
-                        moved = true;
-                    }
+                    lmx[rr] = fmaxf(fmaxf(sc[0][rr], sc[0][rr + 2]), fmaxf(sc[1][rr], sc[1][rr + 2])) * a.scale;
+                    need |= lmx[rr] > m[rr] + 6.0f;
                 }
-                float p[2][4];
+                if (__any_sync(0xffffffffu, need)) {
+                    float alpha[2] = {1.f, 1.f};
 #pragma unroll
-                for (int mt = 0; mt < 2; mt++)
-#pragma unroll
-                    for (int e = 0; e < 4; e++) p[mt][e] = fast_exp2(fmaf(sc[mt][e], a.scale, -m[e & 1]));
-                if (__any_sync(0xffffffffu, moved)) {
+                    for (int rr = 0; rr < 2; rr++) {
+                        float mx = lmx[rr];
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                        if (mx > m[rr] + 6.0f) {
+                            alpha[rr] = fast_exp2(m[rr] - mx);
+                            m[rr] = mx;
+                        }
+                    }
 #pragma unroll
                     for (int rr = 0; rr < 2; rr++) {
                         l_part[rr] *= alpha[rr];
@@ -567,6 +569,11 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
                         acc[i9][3] *= alpha[1];
                     }
                 }
+                float p[2][4];
+#pragma unroll
+                for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+                    for (int e = 0; e < 4; e++) p[mt][e] = fast_exp2(fmaf(sc[mt][e], a.scale, -m[e & 1]));
 #pragma unroll
                 for (int rr = 0; rr < 2; rr++) {
 #pragma unroll

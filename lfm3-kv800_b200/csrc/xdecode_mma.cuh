@@ -231,24 +231,28 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
         s2[1] = (t_a < total) ? sc[1] * a.scale : -__int_as_float(0x7f800000);
         s2[2] = (t_b < total) ? sc[2] * a.scale : -__int_as_float(0x7f800000);
         s2[3] = (t_b < total) ? sc[3] * a.scale : -__int_as_float(0x7f800000);
-        float alpha[2] = {1.f, 1.f};
-        bool moved = false;
+        // the row maxima are reduced across the 8 lanes of a row only when some score of the warp passes its row's
+        // reference point by more than 2^6
+        float lmx[2];
+        bool need = false;
 #pragma unroll
         for (int rr = 0; rr < 2; rr++) {
-            float mx = fmaxf(s2[rr], s2[rr + 2]);
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-            if (mx > m[rr] + 6.0f) {
-                alpha[rr] = fast_exp2(m[rr] - mx);
-                m[rr] = mx;
-                moved = true;
-            }
+            lmx[rr] = fmaxf(s2[rr], s2[rr + 2]);
+            need |= lmx[rr] > m[rr] + 6.0f;
         }
-        float p[4];
+        if (__any_sync(0xffffffffu, need)) {
+            float alpha[2] = {1.f, 1.f};
 #pragma unroll
-        for (int k = 0; k < 4; k++) p[k] = fast_exp2(s2[k] - m[k & 1]);
-        if (__any_sync(0xffffffffu, moved)) {
+            for (int rr = 0; rr < 2; rr++) {
+                float mx = lmx[rr];
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                if (mx > m[rr] + 6.0f) {
+                    alpha[rr] = fast_exp2(m[rr] - mx);
+                    m[rr] = mx;
+                }
+            }
             l_part[0] *= alpha[0];
             l_part[1] *= alpha[1];
 #pragma unroll
@@ -259,6 +263,9 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
                 acc[i][3] *= alpha[1];
             }
         }
+        float p[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) p[k] = fast_exp2(s2[k] - m[k & 1]);
         l_part[0] += p[0] + p[2];
         l_part[1] += p[1] + p[3];
         // ---- PV: B = P^T (hi + lo bf16), A = V^T via ldmatrix.trans

@@ -78,7 +78,7 @@ def test_decode_timed_matches_decode(kv800, tables, win, n):
     K, V, q = I.parity_inputs(win, n)
     st = kv800.PagedStore(2, n + 8, DEV, window=win)
     st.append(tb(K, DEV), tb(V, DEV))
-    c32, s32 = tables
+    _, _, c32, s32 = tables
     ref = nb(kv800.decode(st.paged(), tb(q, DEV), c32, s32, st.H))
     out, ms = kv800.decode_timed(st.paged(), tb(q, DEV), c32, s32)
     assert np.array_equal(nb(out), ref)
