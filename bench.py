@@ -526,6 +526,7 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
+        os.environ.setdefault("NCCL_DEBUG", "WARN")     # keep stdout to the one JSON line
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     if a.workload == "ragged":
