@@ -357,8 +357,8 @@ def flush_bench(kv800, torch, dev, reps=10):
             "prefill_gbs": round(112 * per / t_pre / 1e9, 1),
             "step_flush_subblocks": B, "step_flush_us": round(t_step * 1e6, 1),
             "step_flush_gbs": round(B * per / t_step / 1e9, 1),
-            "bound": "fp32 FMA (16.8 M FMA per sub-block for the bit-exact Hadamard chain)",
-            "fma_tflops": round(2 * 16.8e6 * 112 / t_pre / 1e12, 1)}
+            "bound": "issue: V rotation by a fast Walsh-Hadamard estimate with certified decisions (exact FMA chain "
+                     "only for tokens with an undecided byte or bit), K codes by a certified reciprocal quotient"}
 
 
 def next_rows_bench(kv800, torch, dev, reps=10):

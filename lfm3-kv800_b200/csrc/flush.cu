@@ -230,6 +230,24 @@ __device__ __forceinline__ void load16(const uint16_t* row, int e, float* out) {
 }
 
 
+// 2-bit K code round(fl(d / sc)) clamped to [0, 3] (torch's .round().clamp(0, 3) of the IEEE quotient) from the
+// cheap quotient d * (1 / sc): that is within 3 ulp of the IEEE one, so where it is more than 4e-6 (x max(1, |q|))
+// away from the decision points 0.5, 1.5, 2.5 both round alike; near them (and for non-finite q) the IEEE divide
+// decides.
+__device__ __forceinline__ uint32_t code2(float d, float sc, float inv) {
+    const float q = d * inv;
+    const float tol = 4e-6f * fmaxf(1.0f, fabsf(q));
+    const bool near = fabsf(q - 0.5f) <= tol || fabsf(q - 1.5f) <= tol || fabsf(q - 2.5f) <= tol || !isfinite(q);
+    return near ? round_clamp(__fdiv_rn(d, sc), 3.0f) : round_clamp(q, 3.0f);
+}
+
+// 1-bit code round(fl(d / sc)) clamped to [0, 1], i.e. [fl(d / sc) > 1/2], from the cheap quotient as in code2.
+__device__ __forceinline__ uint32_t code1(float d, float sc, float inv) {
+    const float q = d * inv;
+    const bool near = fabsf(q - 0.5f) <= 4e-6f * fmaxf(1.0f, fabsf(q)) || !isfinite(q);
+    return near ? round_clamp(__fdiv_rn(d, sc), 1.0f) : (q > 0.5f ? 1u : 0u);
+}
+
 template <class Src>
 __global__ void __launch_bounds__(256) flush_kernel(Src src) {
     const int64_t m = blockIdx.x;
@@ -289,6 +307,9 @@ __global__ void __launch_bounds__(256) flush_kernel(Src src) {
                 out[KSC_O + h * DIM + c] = (uint8_t)sc8;
             }
         }
+        float inv[4];
+#pragma unroll
+        for (int p = 0; p < 4; p++) inv[p] = __frcp_rn(scf[p]);
 #pragma unroll 4
         for (int i = 0; i < 32; i++) {
             const int t = grp * 32 + i;
@@ -300,7 +321,7 @@ __global__ void __launch_bounds__(256) flush_kernel(Src src) {
             }
             uint32_t byte = 0;
 #pragma unroll
-            for (int p = 0; p < 4; p++) byte |= round_clamp(__fdiv_rn(x[p] - lof[p], scf[p]), 3.0f) << (2 * p);
+            for (int p = 0; p < 4; p++) byte |= code2(x[p] - lof[p], scf[p], inv[p]) << (2 * p);
             out[KC_O + (t * HEADS + h) * 32 + j] = (uint8_t)byte;
         }
         return;
@@ -326,39 +347,88 @@ __global__ void __launch_bounds__(256) flush_kernel(Src src) {
             for (int i = 0; i < 16; i++) vbuf[warp][h * DIM + e + i] = x[i];
         }
         __syncwarp();
-        float y[HEADS][4];
-        hadamard_rows(vbuf[warp], C, y);
-        __syncwarp();
-        // per 2-head group: lo / hi over 256 dims, fp8 lo and scale hi - lo, 1-bit codes
-        uint32_t part[HEADS];
+        // per 2-head group: lo / hi over 256 dims, fp8 lo and scale hi - lo, 1-bit codes.  First from the fast
+        // transform: every decision is taken at both ends of the error interval [y - E, y + E] (all of them are
+        // monotone in y), and where both ends agree it is the decision the exact chain gives.  A token with any
+        // undecided byte or bit is redone with the exact chain.
+        uint32_t part[HEADS], lo8[2], sc8[2];
+        {
+            float y[HEADS][4], E[HEADS];
+            bool ok = fwht_rows(vbuf[warp], y, E);
 #pragma unroll
-        for (int h = 0; h < HEADS; h++) part[h] = 0;
+            for (int h = 0; h < HEADS; h++) part[h] = 0;
 #pragma unroll
-        for (int g = 0; g < 2; g++) {
-            float l = y[2 * g][0], u = y[2 * g][0];
+            for (int g = 0; g < 2; g++) {
+                const float Eg = fmaxf(E[2 * g], E[2 * g + 1]);
+                float l = y[2 * g][0], u = y[2 * g][0];
 #pragma unroll
-            for (int hh = 0; hh < 2; hh++)
+                for (int hh = 0; hh < 2; hh++)
 #pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    l = fminf(l, y[2 * g + hh][k]);
-                    u = fmaxf(u, y[2 * g + hh][k]);
+                    for (int k = 0; k < 4; k++) {
+                        l = fminf(l, y[2 * g + hh][k]);
+                        u = fmaxf(u, y[2 * g + hh][k]);
+                    }
+#pragma unroll
+                for (int o = 16; o; o >>= 1) {
+                    l = fminf(l, __shfl_xor_sync(0xffffffffu, l, o));
+                    u = fmaxf(u, __shfl_xor_sync(0xffffffffu, u, o));
                 }
+                const float l_lo = __fsub_rd(l, Eg), l_hi = __fadd_ru(l, Eg);
+                const float u_lo = __fsub_rd(u, Eg), u_hi = __fadd_ru(u, Eg);
+                lo8[g] = f8enc(l_lo);
+                sc8[g] = f8enc(clamp_min_1e8(u_lo - l_hi));
+                ok = ok && lo8[g] == f8enc(l_hi) && sc8[g] == f8enc(clamp_min_1e8(u_hi - l_lo));
+                const float lof = f8dec(lo8[g]), scf = clamp_min_1e8(f8dec(sc8[g]));
+                const float inv = __frcp_rn(scf);
+                // bit = [fl(fl(y - lo8) / sc8) > 1/2] for the chain's y, which lies within Eg of the estimate:
+                // decided when the estimate's quotient is farther from 1/2 than Eg / sc8 plus the quotient's own error
+                const float tol = fmaf(Eg, inv * 1.01f, 4e-6f);
 #pragma unroll
-            for (int o = 16; o; o >>= 1) {
-                l = fminf(l, __shfl_xor_sync(0xffffffffu, l, o));
-                u = fmaxf(u, __shfl_xor_sync(0xffffffffu, u, o));
+                for (int hh = 0; hh < 2; hh++)
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const float q = (y[2 * g + hh][k] - lof) * inv;
+                        ok = ok && fabsf(q - 0.5f) > tol * fmaxf(1.0f, fabsf(q));
+                        part[2 * g + hh] |= (q > 0.5f ? 1u : 0u) << ((lane >> 4) + 2 * k);
+                    }
             }
-            uint32_t lo8 = f8enc(l), sc8 = f8enc(clamp_min_1e8(u - l));
-            float lof = f8dec(lo8), scf = clamp_min_1e8(f8dec(sc8));
+            if (!__all_sync(0xffffffffu, ok)) {
+                hadamard_rows(vbuf[warp], C, y);
 #pragma unroll
-            for (int hh = 0; hh < 2; hh++)
+                for (int h = 0; h < HEADS; h++) part[h] = 0;
 #pragma unroll
-                for (int k = 0; k < 4; k++)
-                    part[2 * g + hh] |= round_clamp(__fdiv_rn(y[2 * g + hh][k] - lof, scf), 1.0f)
-                                        << ((lane >> 4) + 2 * k);
-            if (lane == 0) {
-                out[VLO_O + t * 2 + g] = (uint8_t)lo8;
-                out[VSC_O + t * 2 + g] = (uint8_t)sc8;
+                for (int g = 0; g < 2; g++) {
+                    float l = y[2 * g][0], u = y[2 * g][0];
+#pragma unroll
+                    for (int hh = 0; hh < 2; hh++)
+#pragma unroll
+                        for (int k = 0; k < 4; k++) {
+                            l = fminf(l, y[2 * g + hh][k]);
+                            u = fmaxf(u, y[2 * g + hh][k]);
+                        }
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) {
+                        l = fminf(l, __shfl_xor_sync(0xffffffffu, l, o));
+                        u = fmaxf(u, __shfl_xor_sync(0xffffffffu, u, o));
+                    }
+                    lo8[g] = f8enc(l);
+                    sc8[g] = f8enc(clamp_min_1e8(u - l));
+                    const float lof = f8dec(lo8[g]), scf = clamp_min_1e8(f8dec(sc8[g]));
+#pragma unroll
+                    for (int hh = 0; hh < 2; hh++)
+#pragma unroll
+                        for (int k = 0; k < 4; k++)
+                            part[2 * g + hh] |= round_clamp(__fdiv_rn(y[2 * g + hh][k] - lof, scf), 1.0f)
+                                                << ((lane >> 4) + 2 * k);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+#pragma unroll
+            for (int g = 0; g < 2; g++) {
+                out[VLO_O + t * 2 + g] = (uint8_t)lo8[g];
+                out[VSC_O + t * 2 + g] = (uint8_t)sc8[g];
             }
         }
         // byte j of (t, h) holds dims j + 16 i at bit i; lane (j, half) owns i = half + 2k
@@ -435,9 +505,10 @@ __global__ void __launch_bounds__(128) fake_quant_k_kernel(const float* x, int64
     const float scq = f8dec(f8enc(clamp_min_1e8(__fdiv_rn(hi - lo, 3.0f))));
     const float scf = clamp_min_1e8(scq);
     float* oc = out + g * BLK * C + c;
+    const float inv = __frcp_rn(scf);
     for (int t = 0; t < BLK; t++) {
         const float v = col[(int64_t)t * C];
-        const float code = (float)round_clamp(__fdiv_rn(v - lof, scf), 3.0f);
+        const float code = (float)code2(v - lof, scf, inv);
         oc[(int64_t)t * C] = fmaf(code, scq, lof);   // code * sc8 is exact, so this is the reference's mul + add
     }
 }
@@ -475,11 +546,12 @@ __global__ void __launch_bounds__(256) fake_quant_v_kernel(const float* v, int64
         }
         const float lof = f8dec(f8enc(l)), scq = f8dec(f8enc(clamp_min_1e8(u - l)));
         const float scf = clamp_min_1e8(scq);
+        const float inv = __frcp_rn(scf);
 #pragma unroll
         for (int hh = 0; hh < 2; hh++)
 #pragma unroll
             for (int k = 0; k < 4; k++) {
-                const float bit = (float)round_clamp(__fdiv_rn(y[2 * g2 + hh][k] - lof, scf), 1.0f);
+                const float bit = (float)code1(y[2 * g2 + hh][k] - lof, scf, inv);
                 buf[warp][(2 * g2 + hh) * DIM + lane + 32 * k] = fmaf(bit, scq, lof);
             }
     }

@@ -46,6 +46,52 @@ __device__ __forceinline__ void hadamard_rows(const float* rows, const float (&C
     }
 }
 
+// Fast estimate of the same rotation with a rigorous error bound, for decisions that only need the rotated value to
+// within a tolerance (the quantizer's fp8 lo / scale bytes and 1-bit codes).  y[h][k] ~ (x_h @ H)[lane + 32 k] by a
+// fast Walsh-Hadamard transform (7 butterfly levels, 2 in-lane, 5 across lanes) and one multiply by c, and E[h] bounds
+// |y - y_chain| for every element of row h, y_chain being the sequential FMA chain of hadamard_rows:
+//   chain:  128 roundings, each <= u |partial sum| <= u c S          (u = 2^-24, S = sum_i |x_i|)
+//   FWHT:   each level's rounding errors sum to <= u S over the nodes feeding one output (7 levels), plus the final
+//           multiply <= u c |W| <= u c S,
+// so |y - y_chain| <= 136 u c S (1 + 1e-5); E = S * (150 u c) + 1e-38 (the absolute term covers subnormal results).
+// Returns false when some S is not finite (NaN / inf inputs or overflow): the caller then needs the exact chain.
+// Zero results are returned as +0, which is what the chain gives (its accumulator starts at +0).
+__device__ __forceinline__ bool fwht_rows(const float* rows, float (&y)[HEADS][4], float (&E)[HEADS]) {
+    const int lane = threadIdx.x & 31;
+    const float c = 0.0883883461356163f;
+    const float KE = 150.0f * 5.9604644775390625e-08f * 0.0883883461356163f;
+    bool finite = true;
+#pragma unroll
+    for (int h = 0; h < HEADS; h++) {
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) v[k] = rows[h * DIM + lane + 32 * k];
+        float s = (fabsf(v[0]) + fabsf(v[1])) + (fabsf(v[2]) + fabsf(v[3]));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        // dims d = lane + 32 k: bits 5, 6 of d are k (in-lane levels), bits 0..4 are the lane (shuffle levels)
+        float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
+        v[0] = a0 + a2;
+        v[2] = a0 - a2;
+        v[1] = a1 + a3;
+        v[3] = a1 - a3;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const bool upper = (lane & o) != 0;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float other = __shfl_xor_sync(0xffffffffu, v[k], o);
+                v[k] = upper ? other - v[k] : v[k] + other;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++) y[h][k] = v[k] * c + 0.0f;
+        finite = finite && isfinite(s);
+        E[h] = fmaf(s, KE, 1e-38f);
+    }
+    return finite;
+}
+
 __device__ __forceinline__ void hadamard_signs(int lane, float (&C)[32]) {
     const float c = 0.0883883461356163f;   // fp32(1 / sqrt(128)), the entry magnitude of the reference's hadamard()
 #pragma unroll

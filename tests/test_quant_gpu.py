@@ -114,3 +114,38 @@ def test_flush_rejects_out_of_range_offsets(kv800):
     kv800.flush(ep, eoff, ebs, ebs * 256, 256, 128, qp, boff, torch.tensor([0]), torch.tensor([0]), status=status)
     assert int(status.item()) & 1
     assert int(qp.sum().item()) == 0
+
+
+def _stress_v(kind, M, rs):
+    """V rows that probe the quantizer's fast-transform decisions: heavy tails, values far apart in scale, tiny
+    (subnormal-range) values, near-constant rows, exact zeros and ties, and rows sitting on rounding boundaries."""
+    shape = (M, 256, 4, 128)
+    g = rs.standard_normal(shape)
+    if kind == "heavy":
+        v = g / (np.abs(rs.standard_normal(shape)) + 1e-3)
+    elif kind == "scales":
+        v = np.where(rs.random_sample(shape) < 0.05, 300.0 * g, 1e-3 * g)
+    elif kind == "tiny":
+        v = g * 1e-38
+    elif kind == "flat":
+        v = 1.0 + 1e-3 * g
+    elif kind == "ties":
+        v = np.round(g * 2) / 2                      # many exact ties and zeros
+        v[:, ::7] = 0.0
+    else:                                           # "grid": values on a coarse grid, rotated sums hit boundaries
+        v = rs.randint(-3, 4, shape) * 0.0625
+    return I.f32_to_bf16(np.clip(v, -3e38, 3e38).astype(np.float32))
+
+
+@pytest.mark.parametrize("kind", ["heavy", "scales", "tiny", "flat", "ties", "grid"])
+def test_quantizer_stress_matches_oracle(kv800, kind):
+    """Bit-exact against the oracle (the reference's sequential FMA chain) on adversarial V rows: the quantizer takes
+    its V decisions from a fast transform with a proven error bound and redoes undecided tokens with the chain."""
+    rs = np.random.RandomState(hash(kind) % 2**31)
+    M = 24
+    k = I.f32_to_bf16(rs.standard_normal((M, 256, 4, 128)).astype(np.float32))
+    v = _stress_v(kind, M, rs)
+    got = kv800.quantize_blocks(tb(k, DEV), tb(v, DEV)).cpu().numpy()
+    ref = O.quantize_blocks(k, v)
+    bad = np.nonzero((got != ref).any(1))[0]
+    assert bad.size == 0, f"{kind}: sub-blocks {bad[:8].tolist()} differ"
