@@ -175,7 +175,9 @@ KV800_API int kv800_write_exact(uint16_t* epool, int64_t epool_elems, const int6
  * Paged decode.  The record below carries the reference's Paged slots (kv800.py:239-248); pointers are device
  * pointers.  sk / sv / skoff / svoff may be NULL (no sinks).  win = 0: quantized layer, sub-blocks j < min(NQ[b],
  * nqmax) plus exact positions [256 NQ[b], N[b]); win > 0: window layer, exact positions [max(256 NQ[b], N[b] - win),
- * N[b]) plus the sinks (positions < min(nsink, lo, N[b])) when sk is set.
+ * N[b]) plus the sinks (positions < min(nsink, lo, N[b])) when sk is set.  The quantized kernel reads sub-blocks by
+ * TMA: qpool must start 16-byte aligned and BOFF entries be multiples of 128 (the reference's layouts use multiples
+ * of 51,200); a sub-block at another offset is skipped and flagged in the status word.
  */
 typedef struct kv800_paged {
     const uint8_t* qpool; int64_t qpool_bytes;
@@ -194,7 +196,8 @@ typedef struct kv800_paged {
 /*
  * kv800_decode -- replaces kv800.decode(P, q, cos_t, sin_t, H, spb, target) (kv800.py:330-383) with one CUDA
  * backend.  q: (B, 16, 128) bf16 post-RoPE; cos_t / sin_t: (npos, 32) bf16 tables of the 32 rotating frequency pairs
- * (dims d and d + 64 share frequency d, d < 32); out: (B, 16, 128) bf16.  spb: sub-blocks per split (<= 0: chosen by
+ * (dims d and d + 64 share frequency d, d < 32), or both NULL for a layer without quantized sub-blocks whose keys
+ * need no rotation (native sliding layers); out: (B, 16, 128) bf16.  spb: sub-blocks per split (<= 0: chosen by
  * the library).  workspace: device scratch of kv800_decode_workspace_size(...) bytes, 256-byte aligned; its first
  * int is the device status word (0 = clean; set when a range check fires).
  */

@@ -13,6 +13,8 @@
 #include "qdecode_mma.cuh"
 #include "xdecode_mma.cuh"
 
+#include <cudaTypedefs.h>
+
 namespace kv800 {
 
 constexpr float NEG_BIG = -1e30f;   // the reference's initial running max (kv800.py:127)
@@ -214,10 +216,48 @@ extern "C" int64_t kv800_decode_workspace_size(int64_t B, int64_t nqmax, int64_t
     return make_plan(B, nqmax, win, spb).bytes;
 }
 
+// TMA descriptors of the quant pool as rows of 128 bytes: boxes of 64 rows with the 128-byte swizzle (kc rows and
+// vb lines) and boxes of 16 rows without (the scale region).  The pool must start 16-byte aligned; a sub-block at an
+// offset that is not a multiple of 128 is flagged and skipped by the kernel.
+static int make_qmaps(const uint8_t* qpool, int64_t qpool_bytes, QMArgs& qa) {
+    static PFN_cuTensorMapEncodeTiled encode = nullptr;
+    if (!encode) {
+        cudaDriverEntryPointQueryResult qres;
+        void* fn = nullptr;
+        const int rc = cuda_status(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qres),
+                                   "cuTensorMapEncodeTiled lookup");
+        if (rc) return rc;
+        if (qres != cudaDriverEntryPointSuccess || !fn) {
+            set_error("cuTensorMapEncodeTiled is not available from the driver");
+            return KV800_ERR_CUDA;
+        }
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
+    }
+    const int64_t rows = qpool_bytes / 128;
+    if (!qpool || (reinterpret_cast<uintptr_t>(qpool) & 15u) || rows < 16 || rows > 0x7fffffffLL) {
+        set_error("quant pool must be 16-byte aligned and hold between 2 KB and 2^31 x 128 bytes");
+        return KV800_ERR_ARG;
+    }
+    cuuint64_t dims[2] = {128, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {128};
+    cuuint32_t box_rows[2] = {128, 64}, box_sc[2] = {128, 16}, es[2] = {1, 1};
+    CUresult r1 = encode(&qa.tm_rows, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(qpool), dims, strides,
+                         box_rows, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r2 = encode(&qa.tm_sc, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(qpool), dims, strides,
+                         box_sc, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (%d, %d)", (int)r1, (int)r2);
+        return KV800_ERR_CUDA;
+    }
+    return KV800_OK;
+}
+
 static int qdecode_setup() {
     static int done = 0;   // per process; the attribute is per function and device-independent in practice
     if (!done) {
-        int rc = cuda_status(cudaFuncSetAttribute(qdecode_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, QM_SMEM),
+        int rc = cuda_status(cudaFuncSetAttribute(qdecode_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, QM_SMEM_TMA),
                              "qdecode_mma smem attribute");
         if (rc) return rc;
         done = 1;
@@ -327,7 +367,11 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
         if (rc) return rc;
         QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
                   mo, lo, ao, 0, 0, SCALE, status, prefix, B, 0x40804080u, 0x38003800u};
-        qdecode_mma<<<(unsigned)pl.G0, 128, QM_SMEM, st>>>(qa);
+        {
+            const int rcm = make_qmaps(qa.qpool, qa.qpool_bytes, qa);
+            if (rcm) return rcm;
+        }
+        qdecode_mma<<<(unsigned)pl.G0, 128, QM_SMEM_TMA, st>>>(qa);
         rc = cuda_status(cudaGetLastError(), "kv800_decode qdecode");
         if (rc) return rc;
         sm.prefix = prefix;
@@ -342,7 +386,11 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
             if (rc) return rc;
             QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
                       mo, lo, ao, (int)rowslots, (int)spb, SCALE, status, nullptr, B, 0x40804080u, 0x38003800u};
-            qdecode_mma<<<dim3((unsigned)B, (unsigned)pl.ns), 128, QM_SMEM, st>>>(qa);
+        {
+            const int rcm = make_qmaps(qa.qpool, qa.qpool_bytes, qa);
+            if (rcm) return rcm;
+        }
+            qdecode_mma<<<dim3((unsigned)B, (unsigned)pl.ns), 128, QM_SMEM_TMA, st>>>(qa);
             rc = cuda_status(cudaGetLastError(), "kv800_decode qdecode");
             if (rc) return rc;
         }
@@ -418,7 +466,11 @@ extern "C" int kv800_qdecode(const uint16_t* q, const uint8_t* qpool, int64_t qp
     if (rc0) return rc0;
     QMArgs qa{q, qpool, qpool_bytes, boff, boff_stride, NQ, nqmax, cos_t, sin_t, npos,
               mo, lo, ao, (int)(ns + 1), (int)spb, scale, status, nullptr, B, 0x40804080u, 0x38003800u};
-    qdecode_mma<<<dim3((unsigned)B, (unsigned)ns), 128, QM_SMEM, as_stream(stream)>>>(qa);
+        {
+            const int rcm = make_qmaps(qa.qpool, qa.qpool_bytes, qa);
+            if (rcm) return rcm;
+        }
+    qdecode_mma<<<dim3((unsigned)B, (unsigned)ns), 128, QM_SMEM_TMA, as_stream(stream)>>>(qa);
     return cuda_status(cudaGetLastError(), "kv800_qdecode launch");
 }
 

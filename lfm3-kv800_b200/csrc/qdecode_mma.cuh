@@ -12,10 +12,14 @@
 //   The exact V of a quantized token is bits * vs + vl in the Hadamard domain (kv800.py:87-91); vl enters through
 //   lv = sum_t p vl, and combine() applies H once (kv800.py:231-236).
 // Online softmax in the log2 domain per 32-token chunk; partial (m, l, acc + lv) written to the reference's slot
-// layout.  Sub-blocks stream into a two-stage shared-memory ring with cp.async (16-byte chunks, rows XOR-swizzled so
-// the fragment loads are bank-conflict free); per sub-block the CTA first decodes the fp8 scales once (hardware
-// e4m3x2 -> f16x2 conversion) into bf16x2 dequant constants and (vl, vs) pairs in shared memory.
+// layout.  Sub-block halves stream into a two-stage shared-memory ring by TMA (cp.async.bulk.tensor over the quant pool
+// seen as 128-byte rows, the 128-byte swizzle putting chunk c of row t at c ^ (t & 7) so the fragment loads are
+// bank-conflict free), one thread issuing and an mbarrier per stage signalling completion; per sub-block the CTA first
+// decodes the fp8 scales once (hardware e4m3x2 -> f16x2 conversion) into bf16x2 dequant constants and (vl, vs) pairs
+// in shared memory.
 #pragma once
+#include <cuda.h>
+
 #include "kv800_common.cuh"
 
 namespace kv800 {
@@ -47,6 +51,9 @@ struct QMArgs {
     // constants they become immediates that the packed-half instructions cannot encode next to the LOP3's mask, and
     // the compiler re-materializes them with an extra ALU instruction per use (~30 % of the kernel's ALU work).
     uint32_t kbase, vbase;
+    // the quant pool as 128-byte rows, for the TMA loads of a sub-block half: tm_rows boxes of 64 rows with the
+    // 128-byte swizzle (kc rows, vb lines), tm_sc boxes of 16 rows unswizzled (the scale region)
+    CUtensorMap tm_rows, tm_sc;
 };
 
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t orv) { return (a & mask) | orv; }
@@ -204,10 +211,10 @@ __device__ __forceinline__ void token_nope(uint32_t w0, uint32_t w1, const uint4
     }
 }
 
-// ---- shared-memory staging of one sub-block (cp.async, 16-byte chunks, XOR-swizzled rows)
+// ---- shared-memory staging of one sub-block half (TMA, 128-byte swizzle)
 // kc region: token row t (128 B = 8 chunks): chunk c stored at c ^ (t & 7).  vb region: 128-B line L (2 tokens):
 // chunk c stored at c ^ (L & 7).  A warp's fragment loads (8 tokens x one 8- or 2-byte piece of the same head) then
-// hit 8 different bank groups.  Scale region linear.
+// hit 8 different bank groups.  Scale region linear.  Stages start 1024-byte aligned, as the swizzle requires.
 // Stage unit = half a sub-block: the kc rows and vb lines of 128 tokens (+ the 2 KB scale region with the first half).
 constexpr int QM_HALF = BLK / 2;
 constexpr int QM_KC_BYTES = QM_HALF * 128;           // 16 KB of kc rows
@@ -221,29 +228,41 @@ constexpr int QM_SMEM = 2 * QM_STAGE + QM_CST_BYTES + QM_VSL_BYTES;   // 59,392 
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-// 16-byte chunk c of a 128-B row / line r (local to the half) -> its swizzled chunk
-__device__ __forceinline__ int swz(int c) { return (c & ~7) | ((c & 7) ^ ((c >> 3) & 7)); }
-
-// copy half `half` of the sub-block at src into a stage: kc rows, vb lines (both swizzled), and for half 0 the scales
-__device__ __forceinline__ void stage_half(uint8_t* dst, const uint8_t* src, int half, int tid) {
-    // 128 threads: 8 kc chunks, 4 vb chunks and (half 0) one scale chunk each; chunk tid + 128 r swizzles to
-    // swz(tid) + 128 r, so every copy is a fixed offset from two per-thread bases
-    const uint32_t dk = smem_u32(dst) + 16 * swz(tid);
-    const uint8_t* sk = src + half * QM_KC_BYTES + 16 * tid;
-#pragma unroll
-    for (int r = 0; r < QM_KC_BYTES / 16 / 128; r++)
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk + 2048 * r), "l"(sk + 2048 * r) : "memory");
-    const uint8_t* sv = src + VB_O + half * QM_VB_BYTES + 16 * tid;
-#pragma unroll
-    for (int r = 0; r < QM_VB_BYTES / 16 / 128; r++)
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk + ST_VB + 2048 * r), "l"(sv + 2048 * r) : "memory");
-    if (half == 0)
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst) + ST_SC + 16 * tid),
-                     "l"(src + VLO_O + 16 * tid) : "memory");
-}
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+constexpr int QM_SMEM_TMA = 1024 + QM_SMEM + 16;   // 1 KB to align the stages for the swizzle, 2 mbarriers
+
+__device__ __forceinline__ void mbar_init(uint32_t bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tma2d(uint32_t dst, const CUtensorMap* tm, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tm)), "r"(0), "r"(y), "r"(bar) : "memory");
+}
+// issue the TMA loads of half `half` of the sub-block at byte offset off (a multiple of 128) into the stage at dst
+// (1024-aligned): kc rows (2 boxes of 64 rows), vb lines (1 box), and with half 0 the scale region; one thread.
+__device__ __forceinline__ void tma_half(const QMArgs& a, uint32_t dst, uint32_t bar, int64_t off, int half) {
+    const int row = (int)(off >> 7);
+    const uint32_t bytes = QM_KC_BYTES + QM_VB_BYTES + (half ? 0 : QM_SC_BYTES);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+    tma2d(dst, &a.tm_rows, row + half * 128, bar);
+    tma2d(dst + 8192, &a.tm_rows, row + half * 128 + 64, bar);
+    tma2d(dst + ST_VB, &a.tm_rows, row + (VB_O >> 7) + half * 64, bar);
+    if (!half) tma2d(dst + ST_SC, &a.tm_sc, row + (VLO_O >> 7), bar);
+}
+// wait for the phase of the given parity of a stage's mbarrier, at most 2^18 polls; false on time-out
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (int i = 0; i < (1 << 18); i++) {
+        uint32_t done;
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                     "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
 
 // two e4m3 bytes (lo = first) -> two fp32, exact (hardware e4m3 -> f16 conversion)
 __device__ __forceinline__ void e4m3x2_to_f32(uint32_t two, float& lo, float& hi) {
@@ -256,15 +275,15 @@ __device__ __forceinline__ bool sub_ok(const QMArgs& a, int b, int64_t jb, const
     if (jb >= a.boff_stride) return false;
     const int64_t off = a.boff[(int64_t)b * a.boff_stride + jb];
     src = a.qpool + off;
-    return off >= 0 && off + SUB <= a.qpool_bytes && (reinterpret_cast<uintptr_t>(src) & 15u) == 0 &&
-           (jb + 1) * BLK <= a.npos;
+    return off >= 0 && off + SUB <= a.qpool_bytes && (off & 127) == 0 && (jb + 1) * BLK <= a.npos;
 }
 
-__global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* raw0 = smem;
-    uint32_t* cst = reinterpret_cast<uint32_t*>(smem + 2 * QM_STAGE);
-    float2* vsl = reinterpret_cast<float2*>(smem + 2 * QM_STAGE + QM_CST_BYTES);
+__global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QMArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t* raw0 = smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);   // the 128-byte swizzle needs 1 KB alignment
+    uint32_t* cst = reinterpret_cast<uint32_t*>(raw0 + 2 * QM_STAGE);
+    float2* vsl = reinterpret_cast<float2*>(raw0 + 2 * QM_STAGE + QM_CST_BYTES);
+    const uint32_t bar0 = smem_u32(raw0 + 2 * QM_STAGE + QM_CST_BYTES + QM_VSL_BYTES);   // 2 x 8-byte mbarriers
 
     const int tid = threadIdx.x;
     const int h = tid >> 5, lane = tid & 31, g = lane >> 2, tig = lane & 3;
@@ -333,6 +352,14 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
                 bq[ks][hl] = (g < 4) ? v : 0u;
             }
     };
+    if (tid == 0) {
+        mbar_init(bar0);
+        mbar_init(bar0 + 8);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    uint32_t phase = 0;      // bit s: parity of the next phase of stage s's mbarrier
+    int timeouts = 0;
     int qrow = b0;
     load_q(qrow);
     // ---- prologue: sub-blocks 0 and 1 of this split into the two stages
@@ -341,10 +368,8 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
         const uint8_t* src;
         const bool ok0 = n > 0 && sub_ok(a, pre.b, u0 - pre.rs, src);
 #pragma unroll
-        for (int k = 0; k < 2; k++) {
-            if (ok0) stage_half(raw0 + k * QM_STAGE, src, k, tid);
-            cp_commit();
-        }
+        for (int k = 0; k < 2; k++)
+            if (ok0 && tid == 0) tma_half(a, smem_u32(raw0 + k * QM_STAGE), bar0 + 8 * k, src - a.qpool, k);
     }
 
     // per-thread shared-memory offsets inside a 16-token tile starting at a multiple of 16 (the swizzle phase
@@ -433,8 +458,10 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
             ok = sub_ok(a, b, jb, src);
         }
         uint8_t* raw = raw0 + (k & 1) * QM_STAGE;
-        cp_wait<1>();
-        __syncthreads();
+        if (ok) {   // every thread waits for the stage's TMA; the completed phase makes its bytes visible
+            if (!mbar_wait(bar0 + 8 * (k & 1), (phase >> (k & 1)) & 1u)) timeouts++;
+            phase ^= 1u << (k & 1);
+        }
         if (half == 0) {
             if (!ok) {
                 if (tid == 0) flag(a.status, (jb >= a.boff_stride || (jb + 1) * BLK > a.npos) ? ST_TABLE : ST_QPOOL);
@@ -614,11 +641,11 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(QMArgs a) {
             const int i2 = (k + 2) >> 1;
             const uint8_t* src2;
             if (persistent) advance(pre, u0 + i2);
-            if (sub_ok(a, pre.b, u0 + i2 - pre.rs, src2)) stage_half(raw, src2, (k + 2) & 1, tid);
+            if (sub_ok(a, pre.b, u0 + i2 - pre.rs, src2) && tid == 0)
+                tma_half(a, smem_u32(raw), bar0 + 8 * (k & 1), src2 - a.qpool, (k + 2) & 1);
         }
-        cp_commit();
     }
-    cp_wait<0>();
+    if (timeouts && tid == 0) flag(a.status, ST_TIMEOUT);
     flush_partial(slot_of(qrow));
 }
 
