@@ -20,7 +20,8 @@ namespace kv800 {
 constexpr float NEG_BIG = -1e30f;   // the reference's initial running max (kv800.py:127)
 
 // Where the partials of row b live.  Quantized slots: grid mode (prefix == nullptr) b * qstride + s for s < ns;
-// persistent mode c + b for the CTAs c whose unit range meets row b's units [prefix[b], prefix[b + 1]).  Exact slots:
+// persistent mode c + b for the CTAs c whose range of half sub-blocks [c 2W / G, (c + 1) 2W / G) meets row b's
+// halves [2 prefix[b], 2 prefix[b + 1]).  Exact slots:
 // xbase + b * xstride + e for e < nx.
 struct SlotMap {
     int ns;
@@ -84,11 +85,12 @@ __global__ void __launch_bounds__(512) combine_kernel(const float* mo, const flo
         q0 = (int64_t)b * sm.qstride;
         nqs = sm.ns;
     } else {
-        const int64_t W = sm.prefix[sm.B];
-        const int64_t rs = sm.prefix[b], re = sm.prefix[b + 1];
-        if (W > 0 && re > rs) {
-            const int64_t G = min(sm.G0, W);
-            const int64_t cf = ((rs + 1) * G - 1) / W, cl = (re * G - 1) / W;
+        const int64_t W2 = 2 * sm.prefix[sm.B];
+        const int64_t rs = 2 * sm.prefix[b], re = 2 * sm.prefix[b + 1];   // the row's halves [rs, re)
+        if (W2 > 0 && re > rs) {
+            const int64_t G = min(sm.G0, W2);
+            // CTA of half u: the c with floor(c W2 / G) <= u < floor((c + 1) W2 / G), i.e. ((u + 1) G - 1) / W2
+            const int64_t cf = ((rs + 1) * G - 1) / W2, cl = (re * G - 1) / W2;
             q0 = cf + b;
             nqs = cl - cf + 1;
         }
@@ -366,7 +368,7 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
         rc = cuda_status(cudaGetLastError(), "kv800_decode schedule");
         if (rc) return rc;
         QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
-                  mo, lo, ao, 0, 0, SCALE, status, prefix, B, 0x40804080u, 0x38003800u};
+                  mo, lo, ao, 0, 0, SCALE, status, prefix, B, 0x40804080u};
         {
             const int rcm = make_qmaps(qa.qpool, qa.qpool_bytes, qa);
             if (rcm) return rcm;
@@ -385,7 +387,7 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
             rc = qdecode_setup();
             if (rc) return rc;
             QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
-                      mo, lo, ao, (int)rowslots, (int)spb, SCALE, status, nullptr, B, 0x40804080u, 0x38003800u};
+                      mo, lo, ao, (int)rowslots, (int)spb, SCALE, status, nullptr, B, 0x40804080u};
         {
             const int rcm = make_qmaps(qa.qpool, qa.qpool_bytes, qa);
             if (rcm) return rcm;
@@ -465,7 +467,7 @@ extern "C" int kv800_qdecode(const uint16_t* q, const uint8_t* qpool, int64_t qp
     int rc0 = qdecode_setup();
     if (rc0) return rc0;
     QMArgs qa{q, qpool, qpool_bytes, boff, boff_stride, NQ, nqmax, cos_t, sin_t, npos,
-              mo, lo, ao, (int)(ns + 1), (int)spb, scale, status, nullptr, B, 0x40804080u, 0x38003800u};
+              mo, lo, ao, (int)(ns + 1), (int)spb, scale, status, nullptr, B, 0x40804080u};
         {
             const int rcm = make_qmaps(qa.qpool, qa.qpool_bytes, qa);
             if (rcm) return rcm;

@@ -6,9 +6,13 @@
 //        k = bf16(c sc + lo) (kv800.py:86) via one bf16x2 FMA per register pair (c sc + lo is exact before the single
 //        rounding), and for the RoPE dims kr = bf16(fl32(k0 cs - k2 sn)) (torch_decode.py:16-24) in fp32.
 //   PV   acc[d, r] += sum_t V^[t, d] P[t, r]: M = 16 dims (one bit plane of 16 V bytes), N = 8 columns, K = 16 tokens,
-//        fp16 operands.  A = 0.5 + bit * 2^(i - 8) for bit plane i (one LOP3 per register from the packed V bytes);
-//        B = fp16(p * vs), transposed from the QK accumulator layout with movmatrix.  A ninth M-tile of constant 0.5
-//        accumulates 0.5 sum_t B, so sum_t B[t, r] bit[t, d] = (acc_i - acc_S) 2^(8 - i) exactly up to fp32 rounding.
+//        fp16 operands.  A = bit * 2^(i - 24) for bit plane i: the V byte sits in bits 0..7 of an fp16 lane, and
+//        masking one bit leaves the fp16 subnormal of exactly that value (one AND per register, no offset).
+//        B = fp16(p * vs), transposed from the QK accumulator layout with movmatrix.  sum_t B[t, r] bit[t, d] =
+//        acc_i 2^(24 - i), carrying only the accumulation's own rounding.  (An offset encoding such as 0.5 + bit 2^k
+//        with a constant tile subtracted at the end cancels a part of size 0.5 sum B against a result of size
+//        ~ sum B / sqrt(tokens), and amplifies the accumulated fp32 rounding by up to 2^8 per plane: ~10 % rel-L2 at
+//        32K tokens of random data.)
 //   The exact V of a quantized token is bits * vs + vl in the Hadamard domain (kv800.py:87-91); vl enters through
 //   lv = sum_t p vl, and combine() applies H once (kv800.py:231-236).
 // Online softmax in the log2 domain per 32-token chunk; partial (m, l, acc + lv) written to the reference's slot
@@ -42,15 +46,15 @@ struct QMArgs {
     int spb;      // grid mode: sub-blocks per split
     float scale;
     int* status;
-    // persistent mode (prefix != nullptr): CTA c of G = min(gridDim.x, W) takes the flattened units
-    // [c W / G, (c + 1) W / G) of the rows' sub-block lists (prefix[b] = sum of min(NQ, nqmax) over rows < b,
-    // prefix[B] = W) and writes the partial of its segment of row b at slot c + b.
+    // persistent mode (prefix != nullptr): the rows' sub-block lists are flattened (prefix[b] = sum of
+    // min(NQ, nqmax) over rows < b, prefix[B] = W) and cut into 2 W half sub-blocks; CTA c of G = min(gridDim.x, 2 W)
+    // takes the halves [c 2W / G, (c + 1) 2W / G) and writes the partial of its segment of row b at slot c + b.
     const int64_t* prefix;
     int64_t B;
-    // bf16x2 (4, 4) and fp16x2 (0.5, 0.5), the bases of the code encodings.  Passed as values: as compile-time
-    // constants they become immediates that the packed-half instructions cannot encode next to the LOP3's mask, and
-    // the compiler re-materializes them with an extra ALU instruction per use (~30 % of the kernel's ALU work).
-    uint32_t kbase, vbase;
+    // bf16x2 (4, 4), the base of the key code encoding.  Passed as a value: as a compile-time constant it becomes an
+    // immediate that the packed-half instructions cannot encode next to the LOP3's mask, and the compiler
+    // re-materializes it with an extra ALU instruction per use (~30 % of the kernel's ALU work).
+    uint32_t kbase;
     // the quant pool as 128-byte rows, for the TMA loads of a sub-block half: tm_rows boxes of 64 rows with the
     // 128-byte swizzle (kc rows, vb lines), tm_sc boxes of 16 rows unswizzled (the scale region)
     CUtensorMap tm_rows, tm_sc;
@@ -243,15 +247,15 @@ __device__ __forceinline__ void tma2d(uint32_t dst, const CUtensorMap* tm, int y
         ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tm)), "r"(0), "r"(y), "r"(bar) : "memory");
 }
 // issue the TMA loads of half `half` of the sub-block at byte offset off (a multiple of 128) into the stage at dst
-// (1024-aligned): kc rows (2 boxes of 64 rows), vb lines (1 box), and with half 0 the scale region; one thread.
-__device__ __forceinline__ void tma_half(const QMArgs& a, uint32_t dst, uint32_t bar, int64_t off, int half) {
+// (1024-aligned): kc rows (2 boxes of 64 rows), vb lines (1 box), and with `sc` the scale region; one thread.
+__device__ __forceinline__ void tma_half(const QMArgs& a, uint32_t dst, uint32_t bar, int64_t off, int half, bool sc) {
     const int row = (int)(off >> 7);
-    const uint32_t bytes = QM_KC_BYTES + QM_VB_BYTES + (half ? 0 : QM_SC_BYTES);
+    const uint32_t bytes = QM_KC_BYTES + QM_VB_BYTES + (sc ? QM_SC_BYTES : 0);
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
     tma2d(dst, &a.tm_rows, row + half * 128, bar);
     tma2d(dst + 8192, &a.tm_rows, row + half * 128 + 64, bar);
     tma2d(dst + ST_VB, &a.tm_rows, row + (VB_O >> 7) + half * 64, bar);
-    if (!half) tma2d(dst + ST_SC, &a.tm_sc, row + (VLO_O >> 7), bar);
+    if (sc) tma2d(dst + ST_SC, &a.tm_sc, row + (VLO_O >> 7), bar);
 }
 // wait for the phase of the given parity of a stage's mbarrier, at most 2^18 polls; false on time-out
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
@@ -288,8 +292,9 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QM
     const int tid = threadIdx.x;
     const int h = tid >> 5, lane = tid & 31, g = lane >> 2, tig = lane & 3;
 
-    // ---- schedule: this CTA's units [u0, u1) and the row cursor of unit u0
-    int64_t u0, u1;          // units of this CTA
+    // ---- schedule: this CTA's half sub-blocks [h0, h1) (sub-block units h >> 1) and the row cursor of unit h0 >> 1
+    int64_t h0, h1;          // halves of this CTA
+    int64_t u0;              // unit of half h0
     int b0;                  // row of unit u0
     int64_t rs0, re0;        // global unit range of row b0 ([rs0, re0); grid mode: [0, nq))
     int slot_c;              // grid mode: slot = b * nslots + slot_c; persistent: slot = slot_c + b
@@ -301,17 +306,19 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QM
         if (nq > a.nqmax) nq = a.nqmax;
         if (nq < 0) nq = 0;
         u0 = min((int64_t)s * a.spb, nq);
-        u1 = min(u0 + a.spb, nq);
+        h0 = 2 * u0;
+        h1 = 2 * min(u0 + a.spb, nq);
         rs0 = 0;
         re0 = nq;
         slot_c = s;
     } else {
-        const int64_t W = a.prefix[a.B];
-        const int64_t G = min((int64_t)gridDim.x, W);
+        const int64_t W2 = 2 * a.prefix[a.B];
+        const int64_t G = min((int64_t)gridDim.x, W2);
         const int64_t c = blockIdx.x;
         if (c >= G) return;
-        u0 = c * W / G;
-        u1 = (c + 1) * W / G;
+        h0 = c * W2 / G;
+        h1 = (c + 1) * W2 / G;
+        u0 = h0 >> 1;
         // largest b with prefix[b] <= u0 and a nonempty row (prefix[b + 1] > u0)
         int64_t lo_b = 0, hi_b = a.B - 1;
         while (lo_b < hi_b) {
@@ -323,8 +330,8 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QM
         re0 = a.prefix[b0 + 1];
         slot_c = (int)c;
     }
-    const int n = (int)(u1 - u0);
-    // unit i (0 <= i < n) -> (row, sub-block) through a forward-only cursor
+    const int n2 = (int)(h1 - h0);
+    // unit u -> (row, sub-block) through a forward-only cursor
     struct Cursor {
         int b;
         int64_t rs, re;
@@ -362,14 +369,15 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QM
     int timeouts = 0;
     int qrow = b0;
     load_q(qrow);
-    // ---- prologue: sub-blocks 0 and 1 of this split into the two stages
-    // ---- prologue: both halves of the first sub-block into the two stages
-    {
+    // ---- prologue: the CTA's first two halves into the two stages (the first one with its sub-block's scales)
+#pragma unroll 1
+    for (int k = 0; k < 2 && k < n2; k++) {
+        const int64_t hk = h0 + k;
         const uint8_t* src;
-        const bool ok0 = n > 0 && sub_ok(a, pre.b, u0 - pre.rs, src);
-#pragma unroll
-        for (int k = 0; k < 2; k++)
-            if (ok0 && tid == 0) tma_half(a, smem_u32(raw0 + k * QM_STAGE), bar0 + 8 * k, src - a.qpool, k);
+        if (persistent) advance(pre, hk >> 1);
+        if (sub_ok(a, pre.b, (hk >> 1) - pre.rs, src) && tid == 0)
+            tma_half(a, smem_u32(raw0 + k * QM_STAGE), bar0 + 8 * k, src - a.qpool, (int)(hk & 1),
+                     k == 0 || (hk & 1) == 0);
     }
 
     // per-thread shared-memory offsets inside a 16-token tile starting at a multiple of 16 (the swizzle phase
@@ -387,9 +395,9 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QM
     const int vsl_a = 2 * g + (h >> 1), vsl_b = 2 * (g + 8) + (h >> 1);
 
     float m[2] = {-1e30f, -1e30f}, l_part[2] = {0.f, 0.f}, lv_part[2] = {0.f, 0.f};
-    float acc[9][4];
+    float acc[8][4];
 #pragma unroll
-    for (int i = 0; i < 9; i++)
+    for (int i = 0; i < 8; i++)
 #pragma unroll
         for (int e = 0; e < 4; e++) acc[i][e] = 0.f;
 
@@ -420,9 +428,9 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QM
                 float* o = a.ao + row * DIM;
 #pragma unroll
                 for (int i0 = 0; i0 < 8; i0++) {
-                    const float f = __uint_as_float((uint32_t)(135 - i0) << 23);   // 2^(8 - i0)
-                    o[2 * g + 16 * i0] = fmaf(acc[i0][rr] - acc[8][rr], f, lv[rr]);
-                    o[2 * g + 1 + 16 * i0] = fmaf(acc[i0][rr + 2] - acc[8][rr + 2], f, lv[rr]);
+                    const float f = __uint_as_float((uint32_t)(151 - i0) << 23);   // 2^(24 - i0)
+                    o[2 * g + 16 * i0] = fmaf(acc[i0][rr], f, lv[rr]);
+                    o[2 * g + 1 + 16 * i0] = fmaf(acc[i0][rr + 2], f, lv[rr]);
                 }
             }
         }
@@ -432,7 +440,7 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QM
             l_part[rr] = lv_part[rr] = 0.f;
         }
 #pragma unroll
-        for (int i9 = 0; i9 < 9; i9++)
+        for (int i9 = 0; i9 < 8; i9++)
 #pragma unroll
             for (int e9 = 0; e9 < 4; e9++) acc[i9][e9] = 0.f;
     };
@@ -443,17 +451,19 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QM
     int b = 0;
     int64_t jb = 0;
     bool ok = false;
-    for (int k = 0; k < 2 * n; k++) {
-        const int i = k >> 1, half = k & 1;
-        if (half == 0) {
-            if (persistent) advance(cur, u0 + i);
+    for (int k = 0; k < n2; k++) {
+        const int64_t u = (h0 + k) >> 1;
+        const int half = (int)((h0 + k) & 1);
+        const bool fresh = half == 0 || k == 0;   // first stage of a sub-block in this CTA: decode its scales
+        if (fresh) {
+            if (persistent) advance(cur, u);
             if (cur.b != qrow) {                 // segment boundary: the previous row's partial is complete
                 flush_partial(slot_of(qrow));
                 qrow = cur.b;
                 load_q(qrow);
             }
             b = cur.b;
-            jb = u0 + i - cur.rs;
+            jb = u - cur.rs;
             const uint8_t* src;
             ok = sub_ok(a, b, jb, src);
         }
@@ -462,7 +472,7 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QM
             if (!mbar_wait(bar0 + 8 * (k & 1), (phase >> (k & 1)) & 1u)) timeouts++;
             phase ^= 1u << (k & 1);
         }
-        if (half == 0) {
+        if (fresh) {
             if (!ok) {
                 if (tid == 0) flag(a.status, (jb >= a.boff_stride || (jb + 1) * BLK > a.npos) ? ST_TABLE : ST_QPOOL);
             } else {
@@ -518,7 +528,9 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QM
 #pragma unroll
                 for (int mt = 0; mt < 2; mt++) {
                     const int t0 = c0 + 16 * mt;
-                    float sx[4] = {0.f, 0.f, 0.f, 0.f};
+                    // two accumulators (rotated half, NoPE half): the two chains of 4 MMAs do not wait for each
+                    // other, which shortens the latency between the key registers and the scores
+                    float sx[4] = {0.f, 0.f, 0.f, 0.f}, sy[4] = {0.f, 0.f, 0.f, 0.f};
                     {
                         const uint8_t* kt = raw + t0 * 128;
                         const uint2 kwa = *reinterpret_cast<const uint2*>(kt + koff_a);
@@ -549,11 +561,11 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QM
                         }
 #pragma unroll
                         for (int ks = 4; ks < 8; ks++)
-                            mma_bf16(sx, Ra[2 * (ks - 4)], Rb[2 * (ks - 4)], Ra[2 * (ks - 4) + 1], Rb[2 * (ks - 4) + 1],
+                            mma_bf16(sy, Ra[2 * (ks - 4)], Rb[2 * (ks - 4)], Ra[2 * (ks - 4) + 1], Rb[2 * (ks - 4) + 1],
                                      bq[ks][0], bq[ks][1]);
                     }
 #pragma unroll
-                    for (int e = 0; e < 4; e++) sc[mt][e] = sx[e];
+                    for (int e = 0; e < 4; e++) sc[mt][e] = sx[e] + sy[e];
                     const float2 xa = vslh[2 * t0 + vsl_a], xb = vslh[2 * t0 + vsl_b];
                     vlv[mt][0] = xa.x; vsv[mt][0] = xa.y;
                     vlv[mt][1] = xb.x; vsv[mt][1] = xb.y;
@@ -589,7 +601,7 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QM
                         lv_part[rr] *= alpha[rr];
                     }
 #pragma unroll
-                    for (int i9 = 0; i9 < 9; i9++) {
+                    for (int i9 = 0; i9 < 8; i9++) {
                         acc[i9][0] *= alpha[0];
                         acc[i9][1] *= alpha[1];
                         acc[i9][2] *= alpha[0];
@@ -622,27 +634,25 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QM
                     const uint8_t* vt = raw + t0 * 64;
 #pragma unroll
                     for (int q4 = 0; q4 < 4; q4++) v[q4] = *reinterpret_cast<const uint16_t*>(vt + voff[q4]);
-                    const uint32_t wa = __byte_perm(v[0], v[1], 0x2420) << 3;   // byte 2g of (t, t + 1)
-                    const uint32_t wb = __byte_perm(v[0], v[1], 0x2521) << 3;   // byte 2g + 1
-                    const uint32_t wc = __byte_perm(v[2], v[3], 0x2420) << 3;
-                    const uint32_t wd = __byte_perm(v[2], v[3], 0x2521) << 3;
+                    const uint32_t wa = __byte_perm(v[0], v[1], 0x2420);   // byte 2g of (t, t + 1), one per lane
+                    const uint32_t wb = __byte_perm(v[0], v[1], 0x2521);   // byte 2g + 1
+                    const uint32_t wc = __byte_perm(v[2], v[3], 0x2420);
+                    const uint32_t wd = __byte_perm(v[2], v[3], 0x2521);
 #pragma unroll
                     for (int i0 = 0; i0 < 8; i0++) {
-                        const uint32_t msk = 0x00080008u << i0;
-                        mma_f16(acc[i0], lop3_and_or(wa, msk, a.vbase), lop3_and_or(wb, msk, a.vbase),
-                                lop3_and_or(wc, msk, a.vbase), lop3_and_or(wd, msk, a.vbase), b0, b1);
+                        const uint32_t msk = 0x00010001u << i0;
+                        mma_f16(acc[i0], wa & msk, wb & msk, wc & msk, wd & msk, b0, b1);
                     }
-                    mma_f16(acc[8], a.vbase, a.vbase, a.vbase, a.vbase, b0, b1);
                 }
             }
         }
         __syncthreads();   // stage (k & 1) free again (and cst / vsl once the second half is done)
-        if (k + 2 < 2 * n) {
-            const int i2 = (k + 2) >> 1;
+        if (k + 2 < n2) {
+            const int64_t h2 = h0 + k + 2;
             const uint8_t* src2;
-            if (persistent) advance(pre, u0 + i2);
-            if (sub_ok(a, pre.b, u0 + i2 - pre.rs, src2) && tid == 0)
-                tma_half(a, smem_u32(raw), bar0 + 8 * (k & 1), src2 - a.qpool, (k + 2) & 1);
+            if (persistent) advance(pre, h2 >> 1);
+            if (sub_ok(a, pre.b, (h2 >> 1) - pre.rs, src2) && tid == 0)
+                tma_half(a, smem_u32(raw), bar0 + 8 * (k & 1), src2 - a.qpool, (int)(h2 & 1), (h2 & 1) == 0);
         }
     }
     if (timeouts && tid == 0) flag(a.status, ST_TIMEOUT);
