@@ -9,7 +9,8 @@ config).  Sub-blocks and exact pages sit at a seeded random permutation of pool 
 A step = the decode of all 6 layers for the rank's 64 sequences (one token per sequence).  `value` = sequences x
 steps x ranks / max-over-ranks device time (tok/s, weak scaling: 64 sequences per GPU).  `e2e` = the same metric
 through the public API with the step's inputs (6 x q, the current token's K / V) copied from pinned host memory, the
-current token written into its exact page, and the 6 outputs read back, all inside the timed region.  `roofline` =
+current token written into its exact page, and the 6 outputs read back, all inside the timed region (the copies on a
+second stream, overlapped with the neighbouring layers' decode).  `roofline` =
 the quantized-split kernel (the dominant one) timed alone with CUDA events: algorithmic bytes (51,200 per sub-block)
 / duration against the measured HBM copy bandwidth.  `cpu_baseline` = the CPU oracle (a C port of the reference's
 torch decode, OpenMP over (sequence, kv head)) on the 64 sequences, all 6 layers, on this host's cores.
@@ -601,15 +602,34 @@ def main():
         hout = [torch.empty(B, 16, 128, dtype=torch.bfloat16).pin_memory() for _ in layers]
         seqs = torch.arange(B, dtype=torch.int32, device=dev)
         posv = torch.full((B,), a.ctx - 1, dtype=torch.int64, device=dev)
+        # copies run on their own stream: all layers' uploads are queued at the step's start, so layer i + 1's
+        # inputs arrive while layer i decodes, and layer i's output is read back while layer i + 1 decodes.  The
+        # device input buffers are reused across steps: the next step's uploads queue behind this step's last
+        # read-back, which waits for the last decode, so no upload overwrites an input still in use.
+        main, cps = torch.cuda.current_stream(dev), torch.cuda.Stream(dev)
+        dq = [torch.empty_like(q) for q in qs]
+        dk = torch.empty(nl, B, 4, 128, dtype=torch.bfloat16, device=dev)
+        dv = torch.empty_like(dk)
+        ready = [torch.cuda.Event() for _ in layers]
+        done = [torch.cuda.Event() for _ in layers]
 
         def e2e_step():
+            with torch.cuda.stream(cps):
+                for i in range(nl):
+                    dq[i].copy_(hq[i], non_blocking=True)
+                    dk[i].copy_(hk[i], non_blocking=True)
+                    dv[i].copy_(hv[i], non_blocking=True)
+                    ready[i].record(cps)
             for i, L in enumerate(layers):
-                q = hq[i].to(dev, non_blocking=True)
-                k = hk[i].to(dev, non_blocking=True)
-                v = hv[i].to(dev, non_blocking=True)
-                kv800.write_exact(L.epool, L.eoff, EBS, EBS * 256, 256, 128, k, v, seqs, posv)
-                o = kv800.decode(L.P, q, c32, s32)
-                hout[i].copy_(o, non_blocking=True)
+                main.wait_event(ready[i])
+                kv800.write_exact(L.epool, L.eoff, EBS, EBS * 256, 256, 128, dk[i], dv[i], seqs, posv)
+                o = kv800.decode(L.P, dq[i], c32, s32)
+                done[i].record(main)
+                cps.wait_event(done[i])
+                with torch.cuda.stream(cps):
+                    hout[i].copy_(o, non_blocking=True)
+                o.record_stream(cps)
+            main.wait_stream(cps)      # the step ends when its last read-back has landed
             return hout
 
         for _ in range(a.warmup):
