@@ -579,10 +579,10 @@ def main():
     kdur, ldur = statistics.median(kt), statistics.median(lt)
     kbytes = L0.B * L0.nq * SUB
     hbm, peak_kind = peaks()
-    # DRAM traffic of qdecode_mma from one ncu capture on 64 x 16,384 (4,032 sub-blocks: 209.0 MB read + 3.7 MB
+    # DRAM traffic of qdecode_mma from one ncu capture on 64 x 16,384 (4,032 sub-blocks: 209.5 MB read + 5.1 MB
     # written), scaled to this launch by sub-blocks (traffic grows in proportion: reads are the sub-blocks plus
     # the cos / sin rows, writes the split partials)
-    traffic = round((209.0e6 + 3.7e6) * (L0.B * L0.nq) / 4032) if a.ctx == N_CTX and a.seqs == B_PER_GPU else None
+    traffic = round((209.5e6 + 5.1e6) * (L0.B * L0.nq) / 4032) if a.ctx == N_CTX and a.seqs == B_PER_GPU else None
     roofline = {"bound": "hbm", "achieved": round(kbytes / kdur / 1e9, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(kbytes / kdur / 1e9 / hbm, 4), "traffic": traffic, "peak_source": peak_kind,
                 "kernel": "qdecode_mma (+ its 1-CTA schedule scan)", "bytes_per_launch": kbytes,
