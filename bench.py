@@ -456,7 +456,7 @@ def next_rows_bench(kv800, torch, dev, reps=10):
     out["vllm_step"] = {"requests": R, "flushed_subblocks": R // 2, "eager_step_us": round(t_step * 1e6, 1),
                         "graph_step_us": round(t_graph * 1e6, 1) if isinstance(t_graph, float) else t_graph,
                         "decode_only_us": round(t_dec * 1e6, 1),
-                        "launches": "write_slots, flush plan + flush, decode tables, 4 decode kernels"}
+                        "launches": "write_slots, flush plan + flush, decode tables, 3 decode kernels"}
     # ---- prefill / extend history assembly for one 32K request
     r0 = 0
     nq0 = S.nq_of(n_new[r0] - 1)
@@ -560,7 +560,7 @@ def main():
         dist.barrier()
     clocks = clk.summary()
     value = a.seqs * a.steps * n_gpus / t
-    launches_per_step = sum(4 if L.nq else 2 for L in layers)   # qsched + qdecode + xdecode + combine
+    launches_per_step = sum(3 if L.nq else 1 for L in layers)   # qsched + qdecode + xdecode (merge included)
 
     # ---- dominant kernel: qdecode_mma (87.5 % of the decode kernels' device time in the ncu launch list), timed by
     # CUDA events around the quantized phase of one quantized-layer decode (schedule + qdecode_mma) with L2 flushed
@@ -589,7 +589,7 @@ def main():
                 "launch_us": round(kdur * 1e6, 1),
                 "layer_decode": {"bytes": L0.algo_bytes(), "us": round(ldur * 1e6, 1),
                                  "achieved_gbs": round(L0.algo_bytes() / ldur / 1e9, 1),
-                                 "kernels": "qsched + qdecode_mma + xdecode_mma + combine"}}
+                                 "kernels": "qsched + qdecode_mma + xdecode_mma (with the merge of each row's partials)"}}
 
     # ---- end to end through the public API with host buffers
     e2e = None
@@ -752,7 +752,7 @@ def ragged_main(a, kv800, torch, dist, dev, rank, world, local, n_gpus):
                              "kernel": "qdecode_mma (+ its 1-CTA schedule scan), rank 0, layer 0",
                              "bytes_per_launch": kbytes, "launch_us": round(kdur * 1e6, 1)},
                 "cpu_baseline": None, "e2e": None,
-                "gpu_launches": sum(4 if L.nqmax else 2 for L in layers) * a.steps, "clocks": clocks}
+                "gpu_launches": sum(3 if L.nqmax else 1 for L in layers) * a.steps, "clocks": clocks}
         print(json.dumps(line), flush=True)
 
 

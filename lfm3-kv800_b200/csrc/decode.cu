@@ -17,22 +17,6 @@
 
 namespace kv800 {
 
-constexpr float NEG_BIG = -1e30f;   // the reference's initial running max (kv800.py:127)
-
-// Where the partials of row b live.  Quantized slots: grid mode (prefix == nullptr) b * qstride + s for s < ns;
-// persistent mode c + b for the CTAs c whose range of half sub-blocks [c 2W / G, (c + 1) 2W / G) meets row b's
-// halves [2 prefix[b], 2 prefix[b + 1]).  Exact slots:
-// xbase + b * xstride + e for e < nx.
-struct SlotMap {
-    int ns;
-    int64_t qstride;
-    const int64_t* prefix;
-    int64_t B;
-    int64_t G0;
-    int64_t xbase, xstride;
-    int nx;
-};
-
 // prefix[b] = sum over rows < b of clamp(min(NQ, nqmax), 0); prefix[B] = W.  One CTA of 1024 threads.
 __global__ void __launch_bounds__(1024) qsched_kernel(const int32_t* NQ, int64_t nqmax, int64_t B, int64_t* prefix) {
     __shared__ int64_t wsum[32];
@@ -74,74 +58,10 @@ __global__ void __launch_bounds__(1024) qsched_kernel(const int32_t* NQ, int64_t
     if (tid == 0) prefix[B] = carry;
 }
 
-// grid (B), block 512: warp = query row r; lane = dims 4 lane .. 4 lane + 3.
-// o = (sum_{quantized} w_s acc_s) H + sum_{exact} w_s acc_s, w_s = exp2(m_s - max m), out = bf16(o / sum_s w_s l_s)
-// (kv800.py:231-236); a row with no keys at all gives zeros (torch_decode.py:71-72).
-__global__ void __launch_bounds__(512) combine_kernel(const float* mo, const float* lo, const float* ao, SlotMap sm,
+// grid (B), block 128: warp h merges query rows 4 h .. 4 h + 3 of row blockIdx.x (combine.cuh).
+__global__ void __launch_bounds__(128) combine_kernel(const float* mo, const float* lo, const float* ao, SlotMap sm,
                                                       uint16_t* out) {
-    const int b = blockIdx.x, r = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int64_t q0 = 0, nqs = 0;   // quantized slots: grid q0 + s * 1, persistent (c0 + b) + i
-    if (sm.prefix == nullptr) {
-        q0 = (int64_t)b * sm.qstride;
-        nqs = sm.ns;
-    } else {
-        const int64_t W2 = 2 * sm.prefix[sm.B];
-        const int64_t rs = 2 * sm.prefix[b], re = 2 * sm.prefix[b + 1];   // the row's halves [rs, re)
-        if (W2 > 0 && re > rs) {
-            const int64_t G = min(sm.G0, W2);
-            // CTA of half u: the c with floor(c W2 / G) <= u < floor((c + 1) W2 / G), i.e. ((u + 1) G - 1) / W2
-            const int64_t cf = ((rs + 1) * G - 1) / W2, cl = (re * G - 1) / W2;
-            q0 = cf + b;
-            nqs = cl - cf + 1;
-        }
-    }
-    const int64_t x0 = sm.xbase + (int64_t)b * sm.xstride;
-    float M = NEG_BIG;
-    for (int64_t i = 0; i < nqs; i++) M = fmaxf(M, mo[(q0 + i) * QROWS + r]);
-    for (int e = 0; e < sm.nx; e++) M = fmaxf(M, mo[(x0 + e) * QROWS + r]);
-    float L = 0.f, oq[4] = {0.f, 0.f, 0.f, 0.f}, oe[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int64_t i = 0; i < nqs + sm.nx; i++) {
-        const bool isq = i < nqs;
-        const int64_t row = (isq ? q0 + i : x0 + (i - nqs)) * QROWS + r;
-        const float w = exp2f(mo[row] - M);
-        L = fmaf(w, lo[row], L);
-        const float4 x = *reinterpret_cast<const float4*>(ao + row * DIM + 4 * lane);
-        if (isq) {
-            oq[0] = fmaf(w, x.x, oq[0]);
-            oq[1] = fmaf(w, x.y, oq[1]);
-            oq[2] = fmaf(w, x.z, oq[2]);
-            oq[3] = fmaf(w, x.w, oq[3]);
-        } else {
-            oe[0] = fmaf(w, x.x, oe[0]);
-            oe[1] = fmaf(w, x.y, oe[1]);
-            oe[2] = fmaf(w, x.z, oe[2]);
-            oe[3] = fmaf(w, x.w, oe[3]);
-        }
-    }
-    if (nqs > 0) {
-        // 128-point Sylvester Hadamard: dims d = 4 lane + e; stages 1, 2 in-lane, 4 .. 64 across lanes 1 .. 16
-        float a0 = oq[0] + oq[1], a1 = oq[0] - oq[1], a2 = oq[2] + oq[3], a3 = oq[2] - oq[3];
-        oq[0] = a0 + a2; oq[2] = a0 - a2; oq[1] = a1 + a3; oq[3] = a1 - a3;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const bool upper = (lane & o) != 0;
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const float other = __shfl_xor_sync(0xffffffffu, oq[e], o);
-                oq[e] = upper ? other - oq[e] : oq[e] + other;
-            }
-        }
-        const float c = 0.0883883461356163f;
-#pragma unroll
-        for (int e = 0; e < 4; e++) oe[e] = fmaf(oq[e], c, oe[e]);
-    }
-    uint16_t res[4];
-#pragma unroll
-    for (int e = 0; e < 4; e++) res[e] = (L > 0.f) ? f2bf(oe[e] / L) : (uint16_t)0;
-    uint2 pk;
-    pk.x = (uint32_t)res[0] | ((uint32_t)res[1] << 16);
-    pk.y = (uint32_t)res[2] | ((uint32_t)res[3] << 16);
-    *reinterpret_cast<uint2*>(out + ((int64_t)b * QROWS + r) * DIM + 4 * lane) = pk;
+    combine_head(mo, lo, ao, sm, out, blockIdx.x, threadIdx.x >> 5, threadIdx.x & 31);
 }
 
 }  // namespace kv800
@@ -188,11 +108,12 @@ int check_paged(const kv800_paged* P, const char* who) {
 }
 
 // Workspace plan of kv800_decode.  spb > 0: grid splits of spb sub-blocks (ns per row, the reference's sizing);
-// spb <= 0: persistent, G0 CTAs over the flattened sub-block list.  Layout: status word | prefix[B + 1] (persistent)
-// | MO, LO [nslots][16] | AO [nslots][16][128], each 256-byte aligned.
+// spb <= 0: persistent, G0 CTAs over the flattened sub-block list.  Layout: status word | per-row arrival counters
+// int32 [B] (from byte 256; cleared with the status word before every decode) | prefix[B + 1] (persistent) |
+// MO, LO [nslots][16] | AO [nslots][16][128], each 256-byte aligned.
 struct Plan {
     bool persistent;
-    int64_t ns, G0, nslots, prefix_off, mo_off, lo_off, ao_off, bytes;
+    int64_t ns, G0, nslots, cnt_off, prefix_off, mo_off, lo_off, ao_off, bytes;
 };
 
 int64_t up256(int64_t x) { return (x + 255) & ~(int64_t)255; }
@@ -204,7 +125,8 @@ Plan make_plan(int64_t B, int64_t nqmax, int64_t win, int64_t spb) {
     p.ns = (nq > 0 && !p.persistent) ? (nq + spb - 1) / spb : 0;
     p.G0 = p.persistent ? persistent_ctas() : 0;
     p.nslots = p.persistent ? p.G0 + B + B * NX_DEFAULT : B * (p.ns + NX_DEFAULT);
-    p.prefix_off = 256;
+    p.cnt_off = 256;
+    p.prefix_off = up256(p.cnt_off + 4 * B);
     p.mo_off = up256(p.prefix_off + (p.persistent ? (B + 1) * 8 : 0));
     p.lo_off = up256(p.mo_off + p.nslots * QROWS * 4);
     p.ao_off = up256(p.lo_off + p.nslots * QROWS * 4);
@@ -356,7 +278,8 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
     float* mo = reinterpret_cast<float*>(ws + pl.mo_off);
     float* lo = reinterpret_cast<float*>(ws + pl.lo_off);
     float* ao = reinterpret_cast<float*>(ws + pl.ao_off);
-    rc = cuda_status(cudaMemsetAsync(status, 0, sizeof(int), st), "kv800_decode status reset");
+    int* count = reinterpret_cast<int*>(ws + pl.cnt_off);
+    rc = cuda_status(cudaMemsetAsync(status, 0, pl.cnt_off + 4 * B, st), "kv800_decode status / counter reset");
     if (rc) return rc;
     if (ev) cudaEventRecord(ev[0], st);
     SlotMap sm{};
@@ -404,13 +327,11 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
     rc = xdecode_setup();
     if (rc) return rc;
     if (ev) cudaEventRecord(ev[1], st);
-    XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, sm.xbase, sm.xstride, NX_DEFAULT, SCALE, status};
+    // the exact partials; the last of a row's NX_DEFAULT CTAs to finish also merges the row's partials into out
+    XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, sm.xbase, sm.xstride, NX_DEFAULT, SCALE, status, count, sm, out};
     launch_xdecode(xa, dim3((unsigned)B, (unsigned)NX_DEFAULT), st);
     rc = cuda_status(cudaGetLastError(), "kv800_decode xdecode");
-    if (rc) return rc;
     if (ev) cudaEventRecord(ev[2], st);
-    combine_kernel<<<(unsigned)B, 512, 0, st>>>(mo, lo, ao, sm, out);
-    rc = cuda_status(cudaGetLastError(), "kv800_decode combine");
     if (ev) cudaEventRecord(ev[3], st);
     return rc;
 }
@@ -502,7 +423,7 @@ extern "C" int kv800_xdecode(const uint16_t* q, const kv800_paged* P, const uint
     }
     int rcx = xdecode_setup();
     if (rcx) return rcx;
-    XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, ns, ns + 1, 1, scale, status};
+    XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, ns, ns + 1, 1, scale, status, nullptr, SlotMap{}, nullptr};
     launch_xdecode(xa, dim3((unsigned)B, 1), as_stream(stream));
     return cuda_status(cudaGetLastError(), "kv800_xdecode launch");
 }
@@ -528,6 +449,6 @@ extern "C" int kv800_combine(const float* mo, const float* lo, const float* ao, 
     sm.xbase = ns;
     sm.xstride = ns + 1;
     sm.nx = 1;
-    combine_kernel<<<(unsigned)B, 512, 0, as_stream(stream)>>>(mo, lo, ao, sm, out);
+    combine_kernel<<<(unsigned)B, 128, 0, as_stream(stream)>>>(mo, lo, ao, sm, out);
     return cuda_status(cudaGetLastError(), "kv800_combine launch");
 }

@@ -12,10 +12,15 @@
 //            movmatrix, split into bf16 hi + lo (P - hi) so the products keep ~16 bits of P; fp32 accumulate.
 // Online softmax in the log2 domain with a lazily moved reference point (as in qdecode_mma).  The partial (m, l, acc)
 // goes to slot xbase + b xstride + e (the reference's slot ns of row b for the single-split form, kv800.py:224-228).
+// With arrival counters (count != nullptr, zeroed before the launch; gridDim.y == nx), the CTA that completes a row's
+// last exact partial merges all of the row's partials (the quantized ones come from the kernel launched before) into
+// out with combine.cuh's warp merge: its stores are fenced before the counter's atomic add, and the merge reads through
+// L2 after a fence, so a decode needs no separate merge launch.
 // ROPE = false is the native sliding layers' form (keys stored post-RoPE, vllm_attn.py:256-257): the reference passes
 // all-ones / all-zeros tables there, whose rotation returns every key unchanged, so this form drops the table copies
 // and the rotation and gives the same scores.
 #pragma once
+#include "combine.cuh"
 #include "qdecode_mma.cuh"
 
 namespace kv800 {
@@ -34,6 +39,9 @@ struct XMArgs {
     int nx;
     float scale;
     int* status;
+    int* count;        // per-row arrival counters (nullptr: partials only, merged by a separate launch)
+    SlotMap sm;        // with count: where the row's partials live, for the merge
+    uint16_t* out;     // with count: (B, 16, 128) bf16 output
 };
 
 constexpr int XM_TILE = 16;
@@ -79,7 +87,7 @@ __device__ __forceinline__ int xm_off(int r, int c) { return r * 256 + ((c ^ (r 
 
 template <bool ROPE>
 __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(1024) uint8_t smem[];   // the same declaration as qdecode_mma's (one symbol per unit)
     const int b = blockIdx.x, e = blockIdx.y, tid = threadIdx.x;
     const int h = tid >> 5, lane = tid & 31, g = lane >> 2, tig = lane & 3;
     const kv800_paged& P = a.P;
@@ -313,6 +321,17 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
                 o[16 * i + g] = acc[i][rr];
                 o[16 * i + g + 8] = acc[i][rr + 2];
             }
+        }
+    }
+    if (a.count) {   // the last CTA of row b to arrive merges the row (warp h: query rows 4 h .. 4 h + 3)
+        __shared__ int last;
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) last = atomicAdd(a.count + b, 1) == a.nx - 1;
+        __syncthreads();
+        if (last) {
+            __threadfence();
+            combine_head(a.mo, a.lo, a.ao, a.sm, a.out, b, h, lane);
         }
     }
 }

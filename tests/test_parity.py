@@ -74,7 +74,8 @@ def test_split_sizes_agree(kv800, tables, spb):
 @pytest.mark.parametrize("win,n", [(0, 1500), (256, 700)])
 def test_decode_timed_matches_decode(kv800, tables, win, n):
     """kv800.decode_timed (the phase-timed entry the bench uses for its roofline) returns decode()'s exact output and
-    positive phase times (the exact phase always runs; the quantized phase only for quantized layers)."""
+    phase times (the exact phase, which also merges the partials, always runs; the quantized phase only for quantized
+    layers; the merge has no launch of its own, so its phase is the gap between two events)."""
     K, V, q = I.parity_inputs(win, n)
     st = kv800.PagedStore(2, n + 8, DEV, window=win)
     st.append(tb(K, DEV), tb(V, DEV))
@@ -82,6 +83,6 @@ def test_decode_timed_matches_decode(kv800, tables, win, n):
     ref = nb(kv800.decode(st.paged(), tb(q, DEV), c32, s32, st.H))
     out, ms = kv800.decode_timed(st.paged(), tb(q, DEV), c32, s32)
     assert np.array_equal(nb(out), ref)
-    assert ms["exact_ms"] > 0 and ms["combine_ms"] > 0 and ms["quantized_ms"] >= 0
+    assert ms["exact_ms"] > 0 and ms["combine_ms"] >= 0 and ms["quantized_ms"] >= 0
     if win == 0:
         assert ms["quantized_ms"] > 0
