@@ -88,8 +88,9 @@ int64_t persistent_ctas() {
 }
 
 int check_paged(const kv800_paged* P, const char* who) {
-    if (!P || !P->epool || !P->eoff || !P->N || !P->NQ || P->ebs <= 0 || P->eoff_stride <= 0) {
-        set_error("%s: null Paged record / epool / eoff / N / NQ, or non-positive ebs / eoff_stride", who);
+    if (!P || !P->epool || !P->eoff || !P->N || !P->NQ || P->ebs <= 0 || P->ebs > 0x7fffffffLL ||
+        P->eoff_stride <= 0) {
+        set_error("%s: null Paged record / epool / eoff / N / NQ, ebs outside [1, 2^31), or eoff_stride <= 0", who);
         return KV800_ERR_ARG;
     }
     if (P->win < 0 || P->nsink < 0 || P->nqmax < 0) {

@@ -1,10 +1,12 @@
 // Exact-token decode partial on the tensor cores (mma.sync m16n8k16, bf16), sm_100a: the sinks and exact bf16 tokens
 // of one (row b, split e), all 4 kv heads (warp = head), in 16-token tiles.
 //
-//   gather   per tile, 16 tokens x 4 heads x (K row, V row) of 256 B plus the tile's cos / sin rows are copied with
-//            cp.async (16-byte chunks) into a two-stage shared-memory ring; rows are XOR-swizzled by (token & 7) in
-//            16-byte chunks so ldmatrix reads are bank-conflict free.  Rows that fail the range / alignment checks are
-//            zero-filled (cp.async src-size 0) and masked out of the softmax.
+//   gather   per tile, 16 tokens x 4 heads x (K row, V row) of 256 B plus the tile's cos / sin rows (64 B) arrive
+//            by bulk copies (cp.async.bulk, one per row, issued by the thread that owns the row) into a two-stage
+//            shared-memory ring with one mbarrier per stage: every thread arrives once per phase with the bytes of its
+//            own copies, so the phase completes when all of them have landed (bounded wait, flagged on time-out).
+//            Rows sit at a 272-byte pitch, so the 8 rows an ldmatrix reads start in 8 different bank groups.  Rows
+//            that fail the range / alignment checks, or lie past the split's list, are zero-filled by the thread.
 //   QK       A = the tile's K rows via ldmatrix.x4 (dims on K); the RoPE dims (d, d + 64), d < 32, are rotated in
 //            registers with the reference's roundings (torch_decode.py:16-24): fma.rn.f32.bf16 gives
 //            fl32(k0 cs - k2 sn) exactly, cvt.rn.bf16x2 the bf16 rounding.  B = q (bf16, columns 4..7 zero).
@@ -45,10 +47,12 @@ struct XMArgs {
 };
 
 constexpr int XM_TILE = 16;
-constexpr int XM_KV_BYTES = HEADS * XM_TILE * 256;          // one of K / V for a tile: 16 KB
-constexpr int XM_CS_BYTES = XM_TILE * 64;                   // cos (or sin) rows of a tile
-constexpr int XM_STAGE = 2 * XM_KV_BYTES + 2 * XM_CS_BYTES;  // 34,816 B
-constexpr int XM_SMEM = 2 * XM_STAGE;
+constexpr int XM_ROW = 272;                                  // pitch of a 256-byte K or V row in shared memory
+constexpr int XM_HEAD_BYTES = XM_TILE * XM_ROW;              // one head's K (or V) rows of a tile
+constexpr int XM_KV_BYTES = HEADS * XM_HEAD_BYTES;           // one of K / V for a tile: 17,408 B
+constexpr int XM_CS_BYTES = XM_TILE * 64;                    // cos (or sin) rows of a tile
+constexpr int XM_STAGE = 2 * XM_KV_BYTES + 2 * XM_CS_BYTES;  // 36,864 B
+constexpr int XM_SMEM = 2 * XM_STAGE + 16;                   // two stages and their two mbarriers
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -60,9 +64,20 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(addr));
 }
-__device__ __forceinline__ void cp16(uint32_t dst, const void* src, bool valid) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
-                 : "memory");
+// bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) completing on the mbarrier at bar
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+// this thread's arrival on the phase, announcing `bytes` of its bulk copies (0: a plain arrival)
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_init_count(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void zero_row(uint8_t* p, int bytes) {
+    for (int o = 0; o < bytes; o += 16) *reinterpret_cast<uint4*>(p + o) = make_uint4(0u, 0u, 0u, 0u);
 }
 
 // RoPE of one register pair on the A fragment: k0 = (K[d], K[d+1]), k2 = (K[d+64], K[d+65]) of one token row,
@@ -82,8 +97,8 @@ __device__ __forceinline__ void rope_frag(uint32_t& k0, uint32_t& k2, uint32_t c
     k2 = r2;
 }
 
-// smem byte offset of (row r, 16-byte chunk c) in a [16 rows][256 B] swizzled tile
-__device__ __forceinline__ int xm_off(int r, int c) { return r * 256 + ((c ^ (r & 7)) << 4); }
+// smem byte offset of (row r, 16-byte chunk c) in a [16 rows][272 B] tile
+__device__ __forceinline__ int xm_off(int r, int c) { return r * XM_ROW + (c << 4); }
 
 template <bool ROPE>
 __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
@@ -111,11 +126,14 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
     const int64_t total = nsk + (x1 - x0);
     const int ntiles = (int)((total + XM_TILE - 1) / XM_TILE);
 
-    // ---- issue the copies of tile `it` into stage `st`; returns nothing, validity lands in smem (zero rows)
-    // thread = (token tt = tid / 8, row role sub = tid % 8: head sub / 2, K (sub even) or V (odd)); plus one cos / sin
-    // chunk per thread (token tid / 8, table (tid / 4) & 1, chunk tid & 3)
+    const uint32_t bar0 = smem_u32(smem + 2 * XM_STAGE);   // mbarrier of stage s at bar0 + 8 s
+    // ---- issue the copies of tile `it` into stage `st` and arrive on its mbarrier; invalid rows are zero-filled
+    // thread = (token tt = tid / 8, row role sub = tid % 8: head sub / 2, K (sub even) or V (odd)); threads < 32 also
+    // copy one table row (token tid / 2, cos (tid even) or sin)
     auto issue = [&](int it, int st) {
         uint8_t* base = smem + st * XM_STAGE;
+        const uint32_t bar = bar0 + 8 * st;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // earlier generic reads of the stage first
         const int tt = tid >> 3, sub = tid & 7, hh = sub >> 1, isv = sub & 1;
         const int64_t ti = (int64_t)it * XM_TILE + tt;
         const uint16_t* row = P.epool;
@@ -136,9 +154,11 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
                 }
             } else {
                 pos = lo_e + x0 + (ti - nsk);
-                if (pos / P.ebs < P.eoff_stride) {
-                    const int64_t o = P.eoff[(int64_t)b * P.eoff_stride + pos / P.ebs] + hh * P.e_hs +
-                                      (pos % P.ebs) * P.e_ts + (isv ? P.e_v : 0);
+                // positions are below 2^31 (N is int32) and 0 < ebs < 2^31 (checked by the host)
+                const uint32_t eb = (uint32_t)P.ebs, pg = (uint32_t)pos / eb, sl = (uint32_t)pos - pg * eb;
+                if (pg < P.eoff_stride) {
+                    const int64_t o = P.eoff[(int64_t)b * P.eoff_stride + pg] + hh * P.e_hs + (int64_t)sl * P.e_ts +
+                                      (isv ? P.e_v : 0);
                     if (o >= 0 && o + DIM <= P.epool_elems) {
                         row = P.epool + o;
                         ok = true;
@@ -158,20 +178,27 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
                 ok = false;
             }
         }
-        const uint32_t dst = smem_u32(base + isv * XM_KV_BYTES + hh * (XM_TILE * 256));
-#pragma unroll
-        for (int c = 0; c < 16; c++) cp16(dst + xm_off(tt, c), ok ? (const void*)(row + 8 * c) : (const void*)P.epool, ok);
-        // cos / sin rows: token tid / 8 ... one chunk per thread
-        if (ROPE) {
-            const int tc = tid >> 3, which = (tid >> 2) & 1, c4 = tid & 3;
+        uint8_t* dst = base + isv * XM_KV_BYTES + hh * XM_HEAD_BYTES + tt * XM_ROW;
+        uint32_t bytes = ok ? 2 * DIM : 0;
+        // cos / sin rows of the tile's tokens: threads < 32, token tid / 2, cos (even) or sin (odd)
+        const uint16_t* trow = nullptr;
+        uint8_t* tdst = nullptr;
+        if (ROPE && tid < 2 * XM_TILE) {
+            const int tc = tid >> 1, which = tid & 1;
             const int64_t tj = (int64_t)it * XM_TILE + tc;
             int64_t pj = -1;
             if (tj < total) pj = (tj < nsk) ? (s0 + tj) : (lo_e + x0 + (tj - nsk));
-            const bool okc = pj >= 0 && pj < a.npos;
-            const uint16_t* tab = which ? a.sin_t : a.cos_t;
-            const uint32_t d = smem_u32(base + 2 * XM_KV_BYTES + which * XM_CS_BYTES + tc * 64 + c4 * 16);
-            cp16(d, okc ? (const void*)(tab + pj * 32 + c4 * 8) : (const void*)a.cos_t, okc);
+            tdst = base + 2 * XM_KV_BYTES + which * XM_CS_BYTES + tc * 64;
+            if (pj >= 0 && pj < a.npos) {
+                trow = (which ? a.sin_t : a.cos_t) + pj * 32;
+                bytes += 64;
+            }
         }
+        mbar_arrive_tx(bar, bytes);   // before the copies, so the phase cannot complete without them
+        if (ok) bulk_g2s(smem_u32(dst), row, 2 * DIM, bar);
+        else zero_row(dst, 2 * DIM);
+        if (trow) bulk_g2s(smem_u32(tdst), trow, 64, bar);
+        else if (tdst) zero_row(tdst, 64);
     };
 
     // ---- q B fragments (standard dims layout): b0 = q[g][16 ks + 2 tig ..], b1 = q[g][16 ks + 8 + 2 tig ..]
@@ -186,10 +213,16 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
             bq[ks][1] = (g < 4) ? v1 : 0u;
         }
     }
+    if (tid == 0) {
+        mbar_init_count(bar0, 128);
+        mbar_init_count(bar0 + 8, 128);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
     if (ntiles > 0) issue(0, 0);
-    cp_commit();
     if (ntiles > 1) issue(1, 1);
-    cp_commit();
+    uint32_t phase = 0;      // bit s: parity of the next phase of stage s's mbarrier
+    int timeouts = 0;
 
     float m[2] = {-1e30f, -1e30f}, l_part[2] = {0.f, 0.f};
     float acc[8][4];
@@ -202,11 +235,12 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
     const int mi = lane >> 3, ri = lane & 7;
     for (int it = 0; it < ntiles; it++) {
         const int st = it & 1;
-        cp_wait<1>();
-        __syncthreads();
+        if (!mbar_wait(bar0 + 8 * st, (phase >> st) & 1u)) timeouts++;
+        phase ^= 1u << st;
+        __syncthreads();   // the zero-filled rows of other threads
         const uint8_t* base = smem + st * XM_STAGE;
-        const uint32_t kb = smem_u32(base + h * (XM_TILE * 256));
-        const uint32_t vb = smem_u32(base + XM_KV_BYTES + h * (XM_TILE * 256));
+        const uint32_t kb = smem_u32(base + h * XM_HEAD_BYTES);
+        const uint32_t vb = smem_u32(base + XM_KV_BYTES + h * XM_HEAD_BYTES);
         const uint32_t* cs = reinterpret_cast<const uint32_t*>(base + 2 * XM_KV_BYTES);
         const uint32_t* sn = reinterpret_cast<const uint32_t*>(base + 2 * XM_KV_BYTES + XM_CS_BYTES);
         // ---- QK: A fragments of the 8 K-steps (matrices: rows 0-7 / 8-15 x dims +0 / +8)
@@ -293,9 +327,8 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
         }
         __syncthreads();
         if (it + 2 < ntiles) issue(it + 2, st);
-        cp_commit();
     }
-    cp_wait<0>();
+    if (timeouts && tid == 0) flag(a.status, ST_TIMEOUT);
     // ---- partial: rows r = 2 tig, 2 tig + 1 (valid for tig < 2); acc[i] rows d = 16 i + g, 16 i + g + 8
     float l[2];
 #pragma unroll
