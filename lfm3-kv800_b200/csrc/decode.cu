@@ -21,6 +21,7 @@ namespace kv800 {
 __global__ void __launch_bounds__(1024) qsched_kernel(const int32_t* NQ, int64_t nqmax, int64_t B, int64_t* prefix) {
     __shared__ int64_t wsum[32];
     __shared__ int64_t carry;
+    pdl_launch_dependents();   // the quantized-partial kernel may place its CTAs now; it waits for this prefix
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) carry = 0;
     __syncthreads();
@@ -206,9 +207,21 @@ static int xdecode_setup() {
 }
 
 // Launch the exact-token partials: with tables, or (both tables null) the no-rotation form of native sliding layers.
-static void launch_xdecode(const XMArgs& xa, dim3 grid, cudaStream_t st) {
-    if (xa.cos_t) xdecode_mma<true><<<grid, 128, XM_SMEM, st>>>(xa);
-    else xdecode_mma<false><<<grid, 128, XM_SMEM, st>>>(xa);
+// early = programmatic dependent launch: the kernel may start while the one before it in the stream still runs (the
+// exact partials do not read the quantized ones; the merge waits for them).
+static void launch_xdecode(const XMArgs& xa, dim3 grid, cudaStream_t st, bool early = false) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = XM_SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = early ? 1 : 0;
+    if (xa.cos_t) cudaLaunchKernelEx(&cfg, xdecode_mma<true>, xa);
+    else cudaLaunchKernelEx(&cfg, xdecode_mma<false>, xa);
 }
 
 // Tables: both given (16-byte aligned, npos > 0), or both null when nothing quantized is decoded (no rotation).
@@ -297,7 +310,20 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
             const int rcm = make_qmaps(qa.qpool, qa.qpool_bytes, qa);
             if (rcm) return rcm;
         }
-        qdecode_mma<<<(unsigned)pl.G0, 128, QM_SMEM_TMA, st>>>(qa);
+        {   // programmatic dependent launch behind the schedule scan (untimed calls): the CTAs are placed while the
+            // scan runs and wait for its prefix
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)pl.G0);
+            cfg.blockDim = dim3(128);
+            cfg.dynamicSmemBytes = QM_SMEM_TMA;
+            cfg.stream = st;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            at[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = at;
+            cfg.numAttrs = ev ? 0 : 1;
+            cudaLaunchKernelEx(&cfg, qdecode_mma, qa);
+        }
         rc = cuda_status(cudaGetLastError(), "kv800_decode qdecode");
         if (rc) return rc;
         sm.prefix = prefix;
@@ -330,7 +356,8 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
     if (ev) cudaEventRecord(ev[1], st);
     // the exact partials; the last of a row's NX_DEFAULT CTAs to finish also merges the row's partials into out
     XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, sm.xbase, sm.xstride, NX_DEFAULT, SCALE, status, count, sm, out};
-    launch_xdecode(xa, dim3((unsigned)B, (unsigned)NX_DEFAULT), st);
+    // early behind a persistent quantized pass (untimed calls): the exact partials fill the SMs its CTAs leave
+    launch_xdecode(xa, dim3((unsigned)B, (unsigned)NX_DEFAULT), st, pl.persistent && !ev);
     rc = cuda_status(cudaGetLastError(), "kv800_decode xdecode");
     if (ev) cudaEventRecord(ev[2], st);
     if (ev) cudaEventRecord(ev[3], st);

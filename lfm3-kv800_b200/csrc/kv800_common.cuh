@@ -21,6 +21,14 @@ __device__ __forceinline__ void flag(int* status, int bit) {
     if (status) atomicOr(status, bit);
 }
 
+// Programmatic dependent launch (a kernel launched with the programmatic-serialization attribute may start while the
+// kernel before it in the stream still runs).  launch_dependents: this CTA allows the next kernel to start launching
+// (it does once every CTA of this grid has allowed it or exited, so every CTA of this grid is resident by then).
+// wait: block until the kernels this one depends on have completed and their writes are visible; a no-op in a kernel
+// launched without the attribute.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ float bf2f(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
 
 // fp32 -> bf16 bits, round to nearest even (NaN kept quiet).

@@ -299,6 +299,10 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QM
     int64_t rs0, re0;        // global unit range of row b0 ([rs0, re0); grid mode: [0, nq))
     int slot_c;              // grid mode: slot = b * nslots + slot_c; persistent: slot = slot_c + b
     const bool persistent = a.prefix != nullptr;
+    // the exact-partial kernel after this one may start filling the SMs this grid leaves; the schedule prefix comes
+    // from the kernel before it, which may still run
+    pdl_launch_dependents();
+    pdl_wait();
     if (!persistent) {
         b0 = blockIdx.x;
         const int s = blockIdx.y;

@@ -363,6 +363,7 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
         if (tid == 0) last = atomicAdd(a.count + b, 1) == a.nx - 1;
         __syncthreads();
         if (last) {
+            pdl_wait();   // launched early behind the quantized-partial kernel: its partials are complete from here
             __threadfence();
             combine_head(a.mo, a.lo, a.ao, a.sm, a.out, b, h, lane);
         }
