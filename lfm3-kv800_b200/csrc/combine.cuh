@@ -23,10 +23,49 @@ struct SlotMap {
 
 // Merge of query rows 4 h .. 4 h + 3 of row b by one warp, lane = dims 4 lane .. 4 lane + 3:
 // o = (sum_{quantized} w_s acc_s) H + sum_{exact} w_s acc_s, w_s = exp2(m_s - max m), out = bf16(o / sum_s w_s l_s);
-// a row with no keys at all gives zeros (torch_decode.py:71-72).  Partials are read through L2 (ld.global.cg): inside
-// the kernel that wrote some of them, this SM's L1 may hold lines from before they were written.
+// a row with no keys at all gives zeros (torch_decode.py:71-72).  Each group of slots (exact, quantized) is reduced in
+// one pass with a running maximum (a partial whose m exceeds it rescales the sums so far by exp2(M - m)), then the two
+// groups are combined; with wait_quantized the exact group is reduced before waiting for the kernel that writes the
+// quantized partials (programmatic dependent launch).  Partials are read through L2 (ld.global.cg): inside the kernel
+// that wrote some of them, this SM's L1 may hold lines from before they were written.
 __device__ __forceinline__ void combine_head(const float* mo, const float* lo, const float* ao, const SlotMap& sm,
-                                             uint16_t* out, int b, int h, int lane) {
+                                             uint16_t* out, int b, int h, int lane, bool wait_quantized = false) {
+    const int r0 = 4 * h;
+    // one group of slots [s0, s0 + cnt) -> running max M, sum L, weighted acc o of this lane's dims
+    auto reduce = [&](int64_t s0, int64_t cnt, float (&M)[4], float (&L)[4], float (&o)[4][4]) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            M[j] = NEG_BIG;
+            L[j] = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; k++) o[j][k] = 0.f;
+        }
+#pragma unroll 4
+        for (int64_t i = 0; i < cnt; i++) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int64_t row = (s0 + i) * QROWS + r0 + j;
+                const float m = __ldcg(mo + row), l = __ldcg(lo + row);
+                const float4 x = __ldcg(reinterpret_cast<const float4*>(ao + row * DIM + 4 * lane));
+                if (m > M[j]) {   // uniform across the warp: every lane reads the same m
+                    const float sc = exp2f(M[j] - m);
+                    L[j] *= sc;
+#pragma unroll
+                    for (int k = 0; k < 4; k++) o[j][k] *= sc;
+                    M[j] = m;
+                }
+                const float w = exp2f(m - M[j]);
+                L[j] = fmaf(w, l, L[j]);
+                o[j][0] = fmaf(w, x.x, o[j][0]);
+                o[j][1] = fmaf(w, x.y, o[j][1]);
+                o[j][2] = fmaf(w, x.z, o[j][2]);
+                o[j][3] = fmaf(w, x.w, o[j][3]);
+            }
+        }
+    };
+    float Mx[4], Lx[4], ox[4][4];
+    reduce(sm.xbase + (int64_t)b * sm.xstride, sm.nx, Mx, Lx, ox);
+    if (wait_quantized) pdl_wait();
     int64_t q0 = 0, nqs = 0;
     if (sm.prefix == nullptr) {
         q0 = (int64_t)b * sm.qstride;
@@ -42,39 +81,8 @@ __device__ __forceinline__ void combine_head(const float* mo, const float* lo, c
             nqs = cl - cf + 1;
         }
     }
-    const int64_t x0 = sm.xbase + (int64_t)b * sm.xstride;
-    const int r0 = 4 * h;
-    float M[4] = {NEG_BIG, NEG_BIG, NEG_BIG, NEG_BIG};
-    auto max_of = [&](int64_t s) {
-#pragma unroll
-        for (int j = 0; j < 4; j++) M[j] = fmaxf(M[j], __ldcg(mo + s * QROWS + r0 + j));
-    };
-#pragma unroll 4
-    for (int64_t i = 0; i < nqs; i++) max_of(q0 + i);
-#pragma unroll 4
-    for (int e = 0; e < sm.nx; e++) max_of(x0 + e);
-    float L[4] = {0.f, 0.f, 0.f, 0.f}, oq[4][4], oe[4][4];
-#pragma unroll
-    for (int j = 0; j < 4; j++)
-#pragma unroll
-        for (int k = 0; k < 4; k++) oq[j][k] = oe[j][k] = 0.f;
-    auto add = [&](int64_t s, float (&o)[4][4]) {
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int64_t row = s * QROWS + r0 + j;
-            const float w = exp2f(__ldcg(mo + row) - M[j]);
-            L[j] = fmaf(w, __ldcg(lo + row), L[j]);
-            const float4 x = __ldcg(reinterpret_cast<const float4*>(ao + row * DIM + 4 * lane));
-            o[j][0] = fmaf(w, x.x, o[j][0]);
-            o[j][1] = fmaf(w, x.y, o[j][1]);
-            o[j][2] = fmaf(w, x.z, o[j][2]);
-            o[j][3] = fmaf(w, x.w, o[j][3]);
-        }
-    };
-#pragma unroll 4
-    for (int64_t i = 0; i < nqs; i++) add(q0 + i, oq);
-#pragma unroll 4
-    for (int e = 0; e < sm.nx; e++) add(x0 + e, oe);
+    float Mq[4], Lq[4], oq[4][4];
+    reduce(q0, nqs, Mq, Lq, oq);
     if (nqs > 0) {
         // 128-point Sylvester Hadamard: dims d = 4 lane + e; stages 1, 2 in-lane, 4 .. 64 across lanes 1 .. 16
 #pragma unroll
@@ -97,17 +105,19 @@ __device__ __forceinline__ void combine_head(const float* mo, const float* lo, c
                     oq[j][e] = upper ? other - oq[j][e] : oq[j][e] + other;
                 }
         }
-        const float c = 0.0883883461356163f;   // 128^-1/2
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-#pragma unroll
-            for (int e = 0; e < 4; e++) oe[j][e] = fmaf(oq[j][e], c, oe[j][e]);
     }
+    const float c = 0.0883883461356163f;   // 128^-1/2
 #pragma unroll
     for (int j = 0; j < 4; j++) {
+        const float M = fmaxf(Mx[j], Mq[j]);
+        const float sx = exp2f(Mx[j] - M), sq = exp2f(Mq[j] - M);
+        const float L = fmaf(sx, Lx[j], sq * Lq[j]), cq = c * sq;
         uint16_t res[4];
 #pragma unroll
-        for (int e = 0; e < 4; e++) res[e] = (L[j] > 0.f) ? f2bf(oe[j][e] / L[j]) : (uint16_t)0;
+        for (int e = 0; e < 4; e++) {
+            const float o = fmaf(oq[j][e], cq, sx * ox[j][e]);
+            res[e] = (L > 0.f) ? f2bf(o / L) : (uint16_t)0;
+        }
         uint2 pk;
         pk.x = (uint32_t)res[0] | ((uint32_t)res[1] << 16);
         pk.y = (uint32_t)res[2] | ((uint32_t)res[3] << 16);

@@ -17,12 +17,16 @@
 
 namespace kv800 {
 
-// prefix[b] = sum over rows < b of clamp(min(NQ, nqmax), 0); prefix[B] = W.  One CTA of 1024 threads.
-__global__ void __launch_bounds__(1024) qsched_kernel(const int32_t* NQ, int64_t nqmax, int64_t B, int64_t* prefix) {
+// prefix[b] = sum over rows < b of clamp(min(NQ, nqmax), 0); prefix[B] = W.  One CTA of 1024 threads.  Also clears
+// the workspace's status word and per-row arrival counters (zero[0 .. nzero)), so a persistent decode needs no
+// separate reset: the kernels after it touch them only once this one has completed.
+__global__ void __launch_bounds__(1024) qsched_kernel(const int32_t* NQ, int64_t nqmax, int64_t B, int64_t* prefix,
+                                                      int* zero, int64_t nzero) {
     __shared__ int64_t wsum[32];
     __shared__ int64_t carry;
-    pdl_launch_dependents();   // the quantized-partial kernel may place its CTAs now; it waits for this prefix
+    pdl_launch_dependents();   // the quantized-partial kernel may place its CTAs now; it waits for this kernel
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int64_t i = tid; i < nzero; i += 1024) zero[i] = 0;
     if (tid == 0) carry = 0;
     __syncthreads();
     for (int64_t base = 0; base < B; base += 1024) {
@@ -293,15 +297,17 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
     float* lo = reinterpret_cast<float*>(ws + pl.lo_off);
     float* ao = reinterpret_cast<float*>(ws + pl.ao_off);
     int* count = reinterpret_cast<int*>(ws + pl.cnt_off);
-    rc = cuda_status(cudaMemsetAsync(status, 0, pl.cnt_off + 4 * B, st), "kv800_decode status / counter reset");
-    if (rc) return rc;
+    if (!pl.persistent) {   // (the persistent pass clears them in its schedule scan)
+        rc = cuda_status(cudaMemsetAsync(status, 0, pl.cnt_off + 4 * B, st), "kv800_decode status / counter reset");
+        if (rc) return rc;
+    }
     if (ev) cudaEventRecord(ev[0], st);
     SlotMap sm{};
     sm.nx = NX_DEFAULT;
     if (pl.persistent) {
         rc = qdecode_setup();
         if (rc) return rc;
-        qsched_kernel<<<1, 1024, 0, st>>>(P->NQ, P->nqmax, B, prefix);
+        qsched_kernel<<<1, 1024, 0, st>>>(P->NQ, P->nqmax, B, prefix, status, (pl.cnt_off + 4 * B) / 4);
         rc = cuda_status(cudaGetLastError(), "kv800_decode schedule");
         if (rc) return rc;
         QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,

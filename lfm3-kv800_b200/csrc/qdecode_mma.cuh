@@ -299,10 +299,10 @@ __global__ void __launch_bounds__(128, 3) qdecode_mma(const __grid_constant__ QM
     int64_t rs0, re0;        // global unit range of row b0 ([rs0, re0); grid mode: [0, nq))
     int slot_c;              // grid mode: slot = b * nslots + slot_c; persistent: slot = slot_c + b
     const bool persistent = a.prefix != nullptr;
-    // the exact-partial kernel after this one may start filling the SMs this grid leaves; the schedule prefix comes
-    // from the kernel before it, which may still run
-    pdl_launch_dependents();
+    // the schedule prefix (and the cleared status word / counters) come from the kernel before this one, which may
+    // still run; after it, the exact-partial kernel may start filling the SMs this grid leaves
     pdl_wait();
+    pdl_launch_dependents();
     if (!persistent) {
         b0 = blockIdx.x;
         const int s = blockIdx.y;

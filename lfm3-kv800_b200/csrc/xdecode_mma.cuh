@@ -362,10 +362,10 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
         __syncthreads();
         if (tid == 0) last = atomicAdd(a.count + b, 1) == a.nx - 1;
         __syncthreads();
-        if (last) {
-            pdl_wait();   // launched early behind the quantized-partial kernel: its partials are complete from here
+        if (last) {   // (launched early behind the quantized-partial kernel: the merge waits for it after the exact
+                      // group)
             __threadfence();
-            combine_head(a.mo, a.lo, a.ao, a.sm, a.out, b, h, lane);
+            combine_head(a.mo, a.lo, a.ao, a.sm, a.out, b, h, lane, true);
         }
     }
 }
