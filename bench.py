@@ -527,7 +527,10 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        os.environ.setdefault("NCCL_DEBUG", "WARN")     # keep stdout to the one JSON line
+        # NCCL logs to stdout, its version banner included at WARN: send the log to a per-process file so that
+        # rank 0's stdout stays the one JSON line
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        os.environ.setdefault("NCCL_DEBUG_FILE", os.path.join(tempfile.gettempdir(), "nccl.%h.%p.log"))
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
     if a.workload == "ragged":
