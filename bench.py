@@ -41,6 +41,20 @@ EBS, NSINK, WIN, SUB = 64, 4, 256, 51200
 FALLBACK_HBM_GBS = 6650.0
 
 
+def stdout_to_stderr(fn):
+    """Run fn with file descriptor 1 pointed at stderr.  NCCL writes to stdout while it creates a communicator (its
+    version banner, at NCCL_DEBUG=WARN or above), and the bench's stdout must be its one JSON line."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        return fn()
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -527,11 +541,11 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        # NCCL logs to stdout, its version banner included at WARN: send the log to a per-process file so that
-        # rank 0's stdout stays the one JSON line
-        os.environ.setdefault("NCCL_DEBUG", "WARN")
-        os.environ.setdefault("NCCL_DEBUG_FILE", os.path.join(tempfile.gettempdir(), "nccl.%h.%p.log"))
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+        def init():
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+            dist.barrier()   # the communicator is created by now
+        stdout_to_stderr(init)
 
     if a.workload == "ragged":
         return ragged_main(a, kv800, torch, dist, dev, rank, world, local, n_gpus)

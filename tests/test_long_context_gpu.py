@@ -1,5 +1,6 @@
 """Long contexts with diffuse attention: 4 rows x 32,768 tokens (127 sub-blocks + 256 exact tokens per row) of random
-K / V, queries small enough that the softmax spreads over tens of thousands of tokens.  The output is then a small
+K / V, queries small enough that the softmax spreads over tens of thousands of tokens (and, for contrast, large
+enough that a few tokens dominate).  The output is then a small
 average of many V terms of both signs, the regime where the quantized-split kernel's fp32 accumulation error is
 amplified the most; the decode must stay within the north-star bar of the oracle on the same pools, both with the
 persistent schedule and with one split per row (the longest accumulation: 127 sub-blocks in one CTA)."""
@@ -8,7 +9,7 @@ import pytest
 import torch
 
 import inputs as I
-from _util import assert_parity, nb, tb
+from _util import assert_parity_ulp, nb, tb
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -34,7 +35,7 @@ def store():
     return kv800, P, Pn
 
 
-@pytest.mark.parametrize("qscale", [0.25, 2.0])
+@pytest.mark.parametrize("qscale", [0.25, 2.0, 8.0])
 @pytest.mark.parametrize("spb", [None, 127])
 def test_long_context_vs_oracle(store, qscale, spb):
     kv800, P, Pn = store
@@ -43,6 +44,7 @@ def test_long_context_vs_oracle(store, qscale, spb):
     cs, sn = I.rope_tables(N + 64)
     got = nb(kv800.decode(P, tb(q, DEV), tb(cs, DEV), tb(sn, DEV), spb=spb))
     ref = O.decode(Pn, q, cs, sn)
-    rel, mx = assert_parity(got, ref, f"32K rows, q scale {qscale}, spb {spb}")
+    # outputs of the peaked case reach magnitude 4 and more, where one bf16 ulp exceeds 2e-2: max(2e-2, 1 ulp)
+    rel = assert_parity_ulp(got, ref, f"32K rows, q scale {qscale}, spb {spb}")
     # the kernel's own error here is a few 1e-3 of rel-L2 (mostly one-ulp bf16 output flips); well inside the bar
     assert rel < 5e-3, f"rel-L2 {rel:.3e}: accumulation error grew"
