@@ -198,8 +198,9 @@ typedef struct kv800_paged {
  * backend.  q: (B, 16, 128) bf16 post-RoPE; cos_t / sin_t: (npos, 32) bf16 tables of the 32 rotating frequency pairs
  * (dims d and d + 64 share frequency d, d < 32), or both NULL for a layer without quantized sub-blocks whose keys
  * need no rotation (native sliding layers); out: (B, 16, 128) bf16.  spb: sub-blocks per split (<= 0: chosen by
- * the library).  workspace: device scratch of kv800_decode_workspace_size(...) bytes, 256-byte aligned; its first
- * int is the device status word (0 = clean; set when a range check fires).
+ * the library).  workspace: device scratch of kv800_decode_workspace_size(...) bytes, 256-byte aligned, any
+ * contents (the decode clears what it needs); its first int is the device status word (0 = clean; set when a range
+ * check fires).
  */
 KV800_API int64_t kv800_decode_workspace_size(int64_t B, int64_t nqmax, int64_t win, int64_t spb);
 KV800_API int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t, const uint16_t* sin_t,
