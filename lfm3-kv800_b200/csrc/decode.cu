@@ -211,21 +211,28 @@ static int xdecode_setup() {
 }
 
 // Launch the exact-token partials: with tables, or (both tables null) the no-rotation form of native sliding layers.
-// early = programmatic dependent launch: the kernel may start while the one before it in the stream still runs (the
-// exact partials do not read the quantized ones; the merge waits for them).
+// Launch configuration of a 128-thread kernel; early = programmatic dependent launch (the kernel may start while the
+// one before it in the stream still runs, and waits for it with griddepcontrol.wait where it reads its results).
+struct LaunchCfg {
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr;
+    LaunchCfg(dim3 grid, size_t smem, cudaStream_t st, bool early) : cfg{}, attr{} {
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(128);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr.val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = early ? 1 : 0;
+    }
+};
+
+// early: the exact partials do not read the quantized ones (the row merge waits for them)
 static void launch_xdecode(const XMArgs& xa, dim3 grid, cudaStream_t st, bool early = false) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(128);
-    cfg.dynamicSmemBytes = XM_SMEM;
-    cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = early ? 1 : 0;
-    if (xa.cos_t) cudaLaunchKernelEx(&cfg, xdecode_mma<true>, xa);
-    else cudaLaunchKernelEx(&cfg, xdecode_mma<false>, xa);
+    LaunchCfg lc(grid, XM_SMEM, st, early);
+    if (xa.cos_t) cudaLaunchKernelEx(&lc.cfg, xdecode_mma<true>, xa);
+    else cudaLaunchKernelEx(&lc.cfg, xdecode_mma<false>, xa);
 }
 
 // Tables: both given (16-byte aligned, npos > 0), or both null when nothing quantized is decoded (no rotation).
@@ -312,23 +319,12 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
         if (rc) return rc;
         QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
                   mo, lo, ao, 0, 0, SCALE, status, prefix, B, 0x40804080u};
-        {
-            const int rcm = make_qmaps(qa.qpool, qa.qpool_bytes, qa);
-            if (rcm) return rcm;
-        }
-        {   // programmatic dependent launch behind the schedule scan (untimed calls): the CTAs are placed while the
-            // scan runs and wait for its prefix
-            cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3((unsigned)pl.G0);
-            cfg.blockDim = dim3(128);
-            cfg.dynamicSmemBytes = QM_SMEM_TMA;
-            cfg.stream = st;
-            cudaLaunchAttribute at[1];
-            at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-            at[0].val.programmaticStreamSerializationAllowed = 1;
-            cfg.attrs = at;
-            cfg.numAttrs = ev ? 0 : 1;
-            cudaLaunchKernelEx(&cfg, qdecode_mma, qa);
+        const int rcm = make_qmaps(qa.qpool, qa.qpool_bytes, qa);
+        if (rcm) return rcm;
+        {   // behind the schedule scan, early in untimed calls: the CTAs are placed while the scan runs and wait for
+            // its prefix
+            LaunchCfg lc(dim3((unsigned)pl.G0), QM_SMEM_TMA, st, !ev);
+            cudaLaunchKernelEx(&lc.cfg, qdecode_mma, qa);
         }
         rc = cuda_status(cudaGetLastError(), "kv800_decode qdecode");
         if (rc) return rc;
@@ -344,10 +340,8 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
             if (rc) return rc;
             QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
                       mo, lo, ao, (int)rowslots, (int)spb, SCALE, status, nullptr, B, 0x40804080u};
-        {
             const int rcm = make_qmaps(qa.qpool, qa.qpool_bytes, qa);
             if (rcm) return rcm;
-        }
             qdecode_mma<<<dim3((unsigned)B, (unsigned)pl.ns), 128, QM_SMEM_TMA, st>>>(qa);
             rc = cuda_status(cudaGetLastError(), "kv800_decode qdecode");
             if (rc) return rc;
@@ -423,10 +417,8 @@ extern "C" int kv800_qdecode(const uint16_t* q, const uint8_t* qpool, int64_t qp
     if (rc0) return rc0;
     QMArgs qa{q, qpool, qpool_bytes, boff, boff_stride, NQ, nqmax, cos_t, sin_t, npos,
               mo, lo, ao, (int)(ns + 1), (int)spb, scale, status, nullptr, B, 0x40804080u};
-        {
-            const int rcm = make_qmaps(qa.qpool, qa.qpool_bytes, qa);
-            if (rcm) return rcm;
-        }
+    const int rcm = make_qmaps(qa.qpool, qa.qpool_bytes, qa);
+    if (rcm) return rcm;
     qdecode_mma<<<dim3((unsigned)B, (unsigned)ns), 128, QM_SMEM_TMA, as_stream(stream)>>>(qa);
     return cuda_status(cudaGetLastError(), "kv800_qdecode launch");
 }
