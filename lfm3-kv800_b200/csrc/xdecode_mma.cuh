@@ -17,7 +17,9 @@
 // With arrival counters (count != nullptr, zeroed before the launch; gridDim.y == nx), the CTA that completes a row's
 // last exact partial merges all of the row's partials (the quantized ones come from the kernel launched before) into
 // out with combine.cuh's warp merge: its stores are fenced before the counter's atomic add, and the merge reads through
-// L2 after a fence, so a decode needs no separate merge launch.
+// L2 after a fence, so a decode needs no separate merge launch.  Launched early behind the quantized-partial kernel
+// (programmatic dependent launch), the CTAs fill the SMs that kernel's CTAs leave; the merge reduces the exact
+// partials first and waits for the quantized ones (griddepcontrol.wait) only then.
 // ROPE = false is the native sliding layers' form (keys stored post-RoPE, vllm_attn.py:256-257): the reference passes
 // all-ones / all-zeros tables there, whose rotation returns every key unchanged, so this form drops the table copies
 // and the rotation and gives the same scores.
