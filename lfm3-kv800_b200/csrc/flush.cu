@@ -47,12 +47,13 @@ struct PagedSrc {
     int* status;
     __device__ __forceinline__ bool rows(int64_t m, int t, int h, const uint16_t*& kr, const uint16_t*& vr) const {
         int64_t b = seq[m], j = blk[m];
-        int64_t p = j * BLK + t;
-        if (b < 0 || b >= nseq || j < 0 || p / ebs >= eoff_stride) {
+        int64_t p = j * BLK + t, pg, sl;
+        page_split(p, ebs, pg, sl);
+        if (b < 0 || b >= nseq || j < 0 || pg >= eoff_stride) {
             flag(status, ST_TABLE);
             return false;
         }
-        int64_t o = eoff[b * eoff_stride + p / ebs] + h * e_hs + (p % ebs) * e_ts;
+        int64_t o = eoff[b * eoff_stride + pg] + h * e_hs + sl * e_ts;
         if (o < 0 || o + DIM > epool_elems || o + e_v < 0 || o + e_v + DIM > epool_elems) {
             flag(status, ST_EPOOL);
             return false;
@@ -96,12 +97,14 @@ struct VllmSrc {
     __device__ __forceinline__ bool rows(int64_t m, int t, int h, const uint16_t*& kr, const uint16_t*& vr) const {
         const int64_t b = pairs[2 * m], j = pairs[2 * m + 1];
         const int64_t p = j * BLK + t;
-        if (b < 0 || b >= R || p / ebs >= bt_stride) {
+        int64_t pg, sl;
+        page_split(p, ebs, pg, sl);
+        if (b < 0 || b >= R || pg >= bt_stride) {
             flag(status, ST_TABLE);
             return false;
         }
-        const int64_t blk = bt[b * bt_stride + p / ebs];
-        const int64_t o = blk * s0 + h * s1 + (p % ebs) * s2;
+        const int64_t blk = bt[b * bt_stride + pg];
+        const int64_t o = blk * s0 + h * s1 + sl * s2;
         if (blk < 0 || o < 0 || o + 256 > epool_elems) {
             flag(status, ST_EPOOL);
             return false;
@@ -197,7 +200,9 @@ __global__ void write_slots_kernel(uint16_t* epool, int64_t epool_elems, int64_t
     const int h = (int)((row / 2) % HEADS), isv = (int)(row & 1);
     const int64_t sl = slot[i];
     if (sl < 0) return;
-    const int64_t o = (sl / ebs) * s0 + h * s1 + (sl % ebs) * s2 + (isv ? 128 : 0);
+    int64_t blk, r;
+    page_split(sl, ebs, blk, r);
+    const int64_t o = blk * s0 + h * s1 + r * s2 + (isv ? 128 : 0);
     if (o < 0 || o + DIM > epool_elems) {
         if (lane == 0) flag(status, ST_EPOOL);
         return;
@@ -575,11 +580,13 @@ __global__ void write_exact_kernel(uint16_t* epool, int64_t epool_elems, const i
     const int64_t i = row / (HEADS * 2);
     const int h = (int)((row / 2) % HEADS), isv = (int)(row & 1);
     const int64_t b = seq[i], p = pos[i];
-    if (b < 0 || b >= nseq || p < 0 || p / ebs >= eoff_stride) {
+    int64_t pg = 0, sl = 0;
+    if (p >= 0) page_split(p, ebs, pg, sl);
+    if (b < 0 || b >= nseq || p < 0 || pg >= eoff_stride) {
         if (lane == 0) flag(status, ST_TABLE);
         return;
     }
-    const int64_t o = eoff[b * eoff_stride + p / ebs] + h * e_hs + (p % ebs) * e_ts + (isv ? e_v : 0);
+    const int64_t o = eoff[b * eoff_stride + pg] + h * e_hs + sl * e_ts + (isv ? e_v : 0);
     if (o < 0 || o + DIM > epool_elems) {
         if (lane == 0) flag(status, ST_EPOOL);
         return;

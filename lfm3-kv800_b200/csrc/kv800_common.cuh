@@ -31,6 +31,20 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 
 __device__ __forceinline__ float bf2f(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
 
+// Page and slot of position p in pages of ebs tokens, (p / ebs, p % ebs) with C++'s semantics: in 32-bit unsigned
+// arithmetic when 0 <= p, ebs < 2^31 (always, for real caches), in 64-bit otherwise.  A 64-bit division by a value
+// known only at run time is emulated in software and costs several times the 32-bit one.
+__device__ __forceinline__ void page_split(int64_t p, int64_t ebs, int64_t& pg, int64_t& sl) {
+    if (((uint64_t)p | (uint64_t)ebs) <= 0x7fffffffull) {
+        const uint32_t q = (uint32_t)p / (uint32_t)ebs;
+        pg = q;
+        sl = (uint32_t)p - q * (uint32_t)ebs;
+    } else {
+        pg = p / ebs;
+        sl = p % ebs;
+    }
+}
+
 // fp32 -> bf16 bits, round to nearest even (NaN kept quiet).
 __device__ __forceinline__ uint16_t f2bf(float f) {
     uint32_t u = __float_as_uint(f);

@@ -227,11 +227,13 @@ __global__ void prefill_rows_kernel(PrefillArgs a) {
         vr = a.sv + (p * HEADS + h) * DIM;
     } else if (r < a.ns + (a.n0 - a.lo)) {
         p = a.lo + (r - a.ns);
-        if (p / a.ebs >= a.bt_len) {
+        int64_t pg, sl;
+        page_split(p, a.ebs, pg, sl);
+        if (pg >= a.bt_len) {
             if (lane == 0) flag(a.status, ST_TABLE);
             return;
         }
-        const int64_t o = (int64_t)a.bt[p / a.ebs] * a.s0 + h * a.s1 + (p % a.ebs) * a.s2;
+        const int64_t o = (int64_t)a.bt[pg] * a.s0 + h * a.s1 + sl * a.s2;
         if (o < 0 || o + 128 + DIM > a.ecache_elems) {
             if (lane == 0) flag(a.status, ST_EPOOL);
             return;
