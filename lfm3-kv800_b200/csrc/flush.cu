@@ -19,7 +19,10 @@
 namespace kv800 {
 
 // Where the 256 x 4 K / V rows of sub-block m come from and where its 51,200 bytes go.
+// Row sources of the flush kernel.  kDirect: rows() is plain arithmetic, cheaper to evaluate per use than to
+// broadcast; the paged sources look rows up through tables, so each warp resolves its rows once, one per lane.
 struct ContigSrc {
+    static constexpr bool kDirect = true;
     const uint16_t* k;
     const uint16_t* v;
     uint8_t* out;
@@ -33,6 +36,7 @@ struct ContigSrc {
 };
 
 struct PagedSrc {
+    static constexpr bool kDirect = false;
     const uint16_t* epool;
     int64_t epool_elems;
     const int64_t* eoff;
@@ -82,6 +86,7 @@ struct PagedSrc {
 // addressed through qbt.  Sub-block m of the launch is pair m of a device-built list (request, sub-block index); CTAs
 // past the list's count exit.
 struct VllmSrc {
+    static constexpr bool kDirect = false;
     const uint16_t* epool;
     int64_t epool_elems, s0, s1, s2, ebs;
     const int32_t* bt;
@@ -215,6 +220,7 @@ __global__ void write_slots_kernel(uint16_t* epool, int64_t epool_elems, int64_t
 
 constexpr int VSPLIT = 4;               // V-part CTAs per sub-block (64 tokens each)
 constexpr int VTOK = BLK / VSPLIT;
+static_assert(VTOK == 64, "the V part's 8 warps take 8 tokens each (row addresses resolved per lane)");
 
 // 16 bf16 of a row at element offset e (e a multiple of 16), as fp32; vector loads when the row is 16-byte aligned.
 __device__ __forceinline__ void load16(const uint16_t* row, int e, float* out) {
@@ -272,12 +278,28 @@ __global__ void __launch_bounds__(256) flush_kernel(Src src) {
             lo[p] = __int_as_float(0x7f800000);
             hi[p] = -__int_as_float(0x7f800000);
         }
+        // the K row of token grp * 32 + i: for a table-driven source, lane i resolves it once and both passes
+        // broadcast it
+        const uint16_t *kr_l = nullptr, *vr_l = nullptr;
+        uint32_t okm = 0u;
+        if constexpr (!Src::kDirect) okm = __ballot_sync(0xffffffffu, src.rows(m, grp * 32 + lane, h, kr_l, vr_l));
+        auto krow = [&](int i, bool& ok) -> const uint16_t* {
+            if constexpr (Src::kDirect) {
+                const uint16_t *kr, *vr;
+                ok = src.rows(m, grp * 32 + i, h, kr, vr);
+                return kr;
+            } else {
+                ok = (okm >> i) & 1u;
+                return reinterpret_cast<const uint16_t*>(
+                    __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(kr_l), i));
+            }
+        };
 #pragma unroll 4
         for (int i = 0; i < 32; i++) {
-            const int t = grp * 32 + i;
-            const uint16_t *kr, *vr;
+            bool ok;
+            const uint16_t* kr = krow(i, ok);
             float x[4] = {0.f, 0.f, 0.f, 0.f};
-            if (src.rows(m, t, h, kr, vr)) {
+            if (ok) {
 #pragma unroll
                 for (int p = 0; p < 4; p++) x[p] = bf2f(kr[j + 32 * p]);
             }
@@ -318,9 +340,10 @@ __global__ void __launch_bounds__(256) flush_kernel(Src src) {
 #pragma unroll 4
         for (int i = 0; i < 32; i++) {
             const int t = grp * 32 + i;
-            const uint16_t *kr, *vr;
+            bool ok;
+            const uint16_t* kr = krow(i, ok);
             float x[4] = {0.f, 0.f, 0.f, 0.f};
-            if (src.rows(m, t, h, kr, vr)) {
+            if (ok) {
 #pragma unroll
                 for (int p = 0; p < 4; p++) x[p] = bf2f(kr[j + 32 * p]);
             }
@@ -337,14 +360,29 @@ __global__ void __launch_bounds__(256) flush_kernel(Src src) {
     float C[32];
     hadamard_signs(lane, C);
     const int t0 = blockIdx.y * VTOK;
+    // the V rows of this warp's 8 tokens x 4 heads: for a table-driven source, lane L resolves token
+    // t0 + warp + 8 (L & 7), head L >> 3, once
+    const uint16_t *kr_v = nullptr, *vr_v = nullptr;
+    uint32_t okv = 0u;
+    if constexpr (!Src::kDirect)
+        okv = __ballot_sync(0xffffffffu, src.rows(m, t0 + warp + 8 * (lane & 7), lane >> 3, kr_v, vr_v));
     for (int tt = warp; tt < VTOK; tt += 8) {
         const int t = t0 + tt;
         // stage the 4 V rows (512 values) of token t as fp32: lane loads 16 values of head lane / 8
         {
             const int h = lane >> 3, e = (lane & 7) * 16;
             const uint16_t *kr, *vr;
+            bool ok;
+            if constexpr (Src::kDirect) {
+                ok = src.rows(m, t, h, kr, vr);
+            } else {
+                const int from = (lane & 24) | (tt >> 3);
+                vr = reinterpret_cast<const uint16_t*>(
+                    __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(vr_v), from));
+                ok = (okv >> from) & 1u;
+            }
             float x[16];
-            if (src.rows(m, t, h, kr, vr)) load16(vr, e, x);
+            if (ok) load16(vr, e, x);
             else
 #pragma unroll
                 for (int i = 0; i < 16; i++) x[i] = 0.f;
