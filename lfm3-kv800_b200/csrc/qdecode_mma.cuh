@@ -110,10 +110,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
-// bf16 bits of an fp8 e4m3fn byte scaled by 2^e (exact for the scalings used here).
-__device__ __forceinline__ uint32_t f8_to_bf16_scaled(uint32_t b, float pw2) {
-    return (uint32_t)f2bf(f8dec(b) * pw2);
-}
 
 // Dims of register i (0..15) of a token's 16 A registers for thread tig (see the layout comment above the kernel).
 __device__ __forceinline__ void reg_dims(int tig, int i, int& d0, int& d1) {
@@ -231,10 +227,6 @@ constexpr int QM_VSL_BYTES = BLK * 2 * 8;            // [t][group] x (vl, vs) fp
 constexpr int QM_SMEM = 2 * QM_STAGE + QM_CST_BYTES + QM_VSL_BYTES;   // 59,392 B: three CTAs per SM
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 constexpr int QM_SMEM_TMA = 1024 + QM_SMEM + 16;   // 1 KB to align the stages for the swizzle, 2 mbarriers
 
