@@ -98,3 +98,19 @@ def test_vllm_step_host_values():
     assert S.aux_offset(view) == 5 * 25600                              # bf16 elements: after 5 sub-blocks
     flat, ps = S.bf16_flat(view[1:])
     assert ps == S.QPAGE // 2 and flat.numel() == 2 * S.QPAGE // 2 and flat.dtype == torch.bfloat16
+
+
+def test_bench_stdout_stays_one_json_line():
+    """bench.py points file descriptor 1 at stderr while NCCL creates its communicator (NCCL prints its version banner
+    to stdout): output written to fd 1 inside the guard, even by native code, lands on stderr, and stdout is back
+    afterwards for the JSON line."""
+    import os
+    import subprocess
+    import sys
+    code = ("import os, sys; sys.path.insert(0, sys.argv[1]); import bench; "
+            "bench.stdout_to_stderr(lambda: os.write(1, b'NCCL version banner\\n')); print('{\"metric\": 1}')")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code, root], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout == '{"metric": 1}\n'
+    assert "NCCL version banner" in r.stderr
