@@ -214,11 +214,19 @@ KV800_API int kv800_decode(const kv800_paged* P, const uint16_t* q, const uint16
  * inside the library (held on every GPU that loads it until exit); a decode that needs more (see
  * kv800_decode_workspace_size) is rejected with KV800_ERR_RANGE.  The first call on a device looks the array up
  * with that device current, so make it before any stream capture.  All calls share the array: calls that may run
- * at the same time on the GPU race and must be serialized by the caller.  Allocates nothing.
+ * at the same time on the GPU race and must be serialized by the caller.  The device range checks write their
+ * status word into the array; read it with kv800_decode_noalloc_status.  Allocates nothing.
  */
 KV800_API int kv800_decode_noalloc(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t,
                                    const uint16_t* sin_t, int64_t npos, int64_t B, int64_t spb, uint16_t* out,
                                    void* stream);
+
+/*
+ * kv800_decode_noalloc_status -- has no counterpart in the reference.  The device status word of the last
+ * kv800_decode_noalloc call on the current device (it lives in the built-in scratch array, out of the caller's
+ * reach): copies it to *host_value after synchronizing `stream`; returns KV800_ERR_DEVICE when a range check fired.
+ */
+KV800_API int kv800_decode_noalloc_status(int* host_value, void* stream);
 
 /*
  * kv800_decode_timed -- has no counterpart in the reference: kv800_decode with CUDA events around its phases, for

@@ -15,6 +15,8 @@
 
 #include <cudaTypedefs.h>
 
+#include <atomic>
+
 namespace kv800 {
 
 // prefix[b] = sum over rows < b of clamp(min(NQ, nqmax), 0); prefix[B] = W.  One CTA of 1024 threads.  Also clears
@@ -184,30 +186,37 @@ static int make_qmaps(const uint8_t* qpool, int64_t qpool_bytes, QMArgs& qa) {
     return KV800_OK;
 }
 
+// The kernels' shared-memory attributes are set once per device: cudaFuncSetAttribute applies to the current
+// device's context, so a process that decodes on several GPUs sets them on each (flags per device ordinal).
+static int set_smem_once(std::atomic<int>* flags, const char* what, int (*apply)()) {
+    int dev = 0;
+    int rc = cuda_status(cudaGetDevice(&dev), what);
+    if (rc) return rc;
+    if (dev < 0 || dev >= MAX_DEV) return apply();   // beyond the flag table: set it on every call
+    if (flags[dev].load(std::memory_order_acquire)) return KV800_OK;
+    rc = apply();
+    if (!rc) flags[dev].store(1, std::memory_order_release);
+    return rc;
+}
+
 static int qdecode_setup() {
-    static int done = 0;   // per process; the attribute is per function and device-independent in practice
-    if (!done) {
-        int rc = cuda_status(cudaFuncSetAttribute(qdecode_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, QM_SMEM_TMA),
-                             "qdecode_mma smem attribute");
-        if (rc) return rc;
-        done = 1;
-    }
-    return KV800_OK;
+    static std::atomic<int> done[MAX_DEV];
+    return set_smem_once(done, "qdecode_mma smem attribute", [] {
+        return cuda_status(cudaFuncSetAttribute(qdecode_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, QM_SMEM_TMA),
+                           "qdecode_mma smem attribute");
+    });
 }
 
 static int xdecode_setup() {
-    static int done = 0;
-    if (!done) {
+    static std::atomic<int> done[MAX_DEV];
+    return set_smem_once(done, "xdecode_mma smem attribute", [] {
         int rc = cuda_status(cudaFuncSetAttribute(xdecode_mma<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                   XM_SMEM),
                              "xdecode_mma smem attribute");
         if (rc) return rc;
-        rc = cuda_status(cudaFuncSetAttribute(xdecode_mma<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, XM_SMEM),
-                         "xdecode_mma smem attribute");
-        if (rc) return rc;
-        done = 1;
-    }
-    return KV800_OK;
+        return cuda_status(cudaFuncSetAttribute(xdecode_mma<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, XM_SMEM),
+                           "xdecode_mma smem attribute");
+    });
 }
 
 // Launch the exact-token partials: with tables, or (both tables null) the no-rotation form of native sliding layers.

@@ -49,6 +49,7 @@ SIGNATURES = {
     "kv800_decode_timed": (_int, [ctypes.POINTER(Paged), _p, _p, _p, _i64, _i64, _i64, _p, _p, _i64, _p,
                                   ctypes.POINTER(ctypes.c_float)]),
     "kv800_decode_noalloc": (_int, [ctypes.POINTER(Paged), _p, _p, _p, _i64, _i64, _i64, _p, _p]),
+    "kv800_decode_noalloc_status": (_int, [_p, _p]),
     "kv800_qdecode": (_int, [_p, _p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _f, _p,
                              _p]),
     "kv800_xdecode": (_int, [_p, ctypes.POINTER(Paged), _p, _p, _i64, _p, _p, _p, _i64, _i64, _f, _p, _p]),

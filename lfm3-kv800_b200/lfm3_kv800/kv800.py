@@ -27,6 +27,7 @@ import os
 import torch
 
 from . import _lib, get_logger
+from . import ops as _ops
 
 BLK, LAG, NSINK, WIN = 256, 128, 4, 256
 SUB = 51200
@@ -35,6 +36,7 @@ F8 = torch.float8_e4m3fn
 LOG2E = 1.4426950408889634
 BACKENDS = ("cuda",)
 _log = get_logger()
+_ops.register()          # torch.ops.kv800.{qdecode, xdecode, combine}: the reference's op schema on these kernels
 
 __all__ = ["BLK", "LAG", "NSINK", "WIN", "SUB", "KC_O", "VB_O", "VLO_O", "VSC_O", "KLO_O", "KSC_O", "F8", "LOG2E",
            "BACKENDS", "hadamard", "flat", "quantize_blocks", "dequantize_blocks", "Paged", "PagedStore", "decode",
