@@ -108,8 +108,10 @@ def _run_schedule(kv800, S, va, ctx):
             for side in ("ref", "ours")}
 
     def qview(t):
-        return torch.as_strided(t, (NQPG, 2, S.QBLOCK, 4, S.QCONTENT),
-                                (S.QPAGE, S.QBLOCK * 4 * S.QCONTENT, 4 * S.QCONTENT, S.QCONTENT, 1))
+        # pages of 262,144 B holding (2, 1280 tokens, 4 heads x 25 B): the reference views a host's page as bf16 for
+        # the sink rows of its aux area, so the last dimension is the 4 heads' 100 bytes of a token
+        return torch.as_strided(t, (NQPG, 2, S.QBLOCK, 4 * S.QCONTENT),
+                                (S.QPAGE, S.QBLOCK * 4 * S.QCONTENT, 4 * S.QCONTENT, 1))
     qv = {side: {l: qview(qraw[side][l]) for l in qbt} for side in qraw}
     for l in LAYERS:
         ref_attn[l].xc.kv_cache = ev["ref"][l]

@@ -12,7 +12,7 @@ import pytest
 import torch
 
 import inputs as I
-from _util import assert_parity, nb, tb
+from _util import assert_parity, assert_parity_ulp, nb, tb
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -63,7 +63,8 @@ def test_noalloc_matches_workspace_decode_twice(win, n, spb):
     for call in range(2):
         got = _noalloc(L, kv800, st, qd, c32, s32, spb)
         assert_parity(got, ref, f"no-alloc decode vs kv800_decode, call {call + 1}")
-        assert_parity(got, oracle, f"no-alloc decode vs oracle, call {call + 1}")
+        # these synthetic outputs reach magnitude 4, where one bf16 ulp exceeds 2e-2: max(2e-2, 1 ulp) per element
+        assert_parity_ulp(got, oracle, f"no-alloc decode vs oracle, call {call + 1}")
 
 
 def test_noalloc_large_then_small():
@@ -80,7 +81,7 @@ def test_noalloc_large_then_small():
         gs = _noalloc(L, kv800, small, tb(qs, DEV), c32, s32, spb)
         assert_parity(gb, nb(kv800.decode(big.paged(), tb(qb, DEV), c32, s32, spb=spb or None)), f"large, spb {spb}")
         assert_parity(gs, nb(kv800.decode(small.paged(), tb(qs, DEV), c32, s32, spb=spb or None)), f"small, spb {spb}")
-    assert_parity(gs, _oracle(small, qs, cs, sn), "small vs oracle")
+    assert_parity_ulp(gs, _oracle(small, qs, cs, sn), "small vs oracle")
 
 
 def test_noalloc_rejects_oversized_decode():
