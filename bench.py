@@ -876,6 +876,12 @@ def main():
                 "layer_decode": {"bytes": L0.algo_bytes(), "us": round(ldur * 1e6, 1),
                                  "achieved_gbs": round(L0.algo_bytes() / ldur / 1e9, 1),
                                  "kernels": "qsched + qdecode_mma + xdecode_mma (with the merge of each row's partials)"}}
+    # a window layer (4 sinks + 256 exact tokens per row): xdecode_mma with each row's merge, L2 flushed
+    LW, qw = layers[QUANT_LAYERS], qs[QUANT_LAYERS]
+    _, wdur = kernel_roofline(kv800, torch, dev, LW, qw, c32, s32)
+    window = {"bytes": LW.algo_bytes(), "us": round(wdur * 1e6, 1),
+              "achieved_gbs": round(LW.algo_bytes() / wdur / 1e9, 1), "frac": round(LW.algo_bytes() / wdur / 1e9 / hbm, 4),
+              "kernel": "xdecode_mma with each row's merge, one window layer, L2 flushed"}
 
     # ---- end to end through the public API with host buffers
     e2e = None
@@ -937,7 +943,8 @@ def main():
                            "timing": window_summary(wins, a.steps)},
                 "hbm_gbs_step": round(step_bytes * a.steps / t / 1e9, 1),
                 "hbm_frac_step": round(step_bytes * a.steps / t / 1e9 / hbm, 4),
-                "bytes_per_step_per_gpu": step_bytes, "roofline": roofline, "parity": parity, "cpu_baseline": cpu,
+                "bytes_per_step_per_gpu": step_bytes, "roofline": roofline, "window_layer": window, "parity": parity,
+                "cpu_baseline": cpu,
                 "cpu_baseline_port": cpu_port, "e2e": e2e,
                 "gpu_launches": launches_per_step * a.steps, "clocks": clocks, "config1": cfg1, "flush": flush,
                 "ragged": ragged, "next_rows": nxt}
