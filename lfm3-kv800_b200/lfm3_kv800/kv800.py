@@ -171,10 +171,15 @@ def write_exact(epool, eoff, ebs, e_hs, e_ts, e_v, k, v, seq, pos, status=None):
 
 # ---------------------------------------------------------------- decode input record (kv800.py:239-248)
 class Paged:
-    """Everything the decode kernels read for one layer and one batch of decode sequences.
-    qpool: uint8 tensor whose data_ptr is the byte base of BOFF; epool: bf16 tensor, base of EOFF (elements);
-    sk/sv: bf16 tensors, bases of SKOFF/SVOFF (elements). N: seq lengths incl. the current token; NQ: flushed
-    sub-blocks per sequence; nqmax: host int >= max(NQ). win: 0 = quantized layer, 256 = window+sinks layer."""
+    """The decode's view of one layer's cache for a batch of rows (the reference's 16-slot record).
+
+    Offsets are relative to the first element of the tensor they index into:
+      qpool  uint8 pool of sub-blocks; boff[b, j] = byte offset of row b's sub-block j
+      epool  bf16 pool of exact pages; eoff[b, p] = element offset of the page holding row b's positions
+             [p ebs, (p + 1) ebs); K of (head h, slot t) at + h e_hs + t e_ts, V at + e_v from K
+      sk, sv bf16 sink pools (window layers); skoff[b] / svoff[b] = element offset of row b's [4, 4, 128] sink rows
+      N      int32 row lengths, the current token included; NQ int32 sub-blocks flushed per row
+      nqmax  host int, an upper bound of NQ; win 0 for a quantized layer, 256 for a window layer with sinks."""
     __slots__ = ("qpool", "boff", "epool", "eoff", "ebs", "e_hs", "e_ts", "e_v", "sk", "sv", "skoff", "svoff",
                  "N", "NQ", "nqmax", "win")
 
@@ -346,10 +351,11 @@ def combine(MO, LO, AO, ns, H=None):
 
 # ---------------------------------------------------------------- harness store with the paged layout (kv800.py:387)
 class PagedStore:
-    """Test/bench store with the vLLM-style paged layout for `batch` equal-length sequences. Exact pages form a ring of
-    `nring` pages of `ebs` tokens per sequence (the window manager's job in vLLM). Same flush rule as the vLLM cache.
-    New tokens are scattered into the exact pages by the CUDA write kernel and eligible sub-blocks are quantized from
-    the pages by the CUDA flush kernel, one launch each per 128-token slice."""
+    """A cache for `batch` rows that all grow together, laid out like the vLLM pages (the reference's test and
+    benchmark harness, kv800.py:387-441).  Each row's exact tokens live in a ring of `nring` pages of `ebs` tokens
+    (vLLM's sliding window frees older pages the same way), its sub-blocks at fixed slots of `qpool`.  append() writes
+    new tokens into the pages with the CUDA scatter kernel and, whenever a row's length reaches 256 j + 384, quantizes
+    sub-block j from the pages with the CUDA flush kernel (one launch per 128-token slice of the appended tokens)."""
 
     def __init__(self, batch, max_len, device, window=0, ebs=64, nring=10):
         device = torch.device(device)
