@@ -875,13 +875,13 @@ def main():
                 "launch_us": round(kdur * 1e6, 1),
                 "layer_decode": {"bytes": L0.algo_bytes(), "us": round(ldur * 1e6, 1),
                                  "achieved_gbs": round(L0.algo_bytes() / ldur / 1e9, 1),
-                                 "kernels": "qsched + qdecode_mma + xdecode_mma (with the merge of each row's partials)"}}
-    # a window layer (4 sinks + 256 exact tokens per row): xdecode_mma with each row's merge, L2 flushed
+                                 "kernels": "qsched + qdecode_mma + xdecode_tma (with the merge of each row's partials)"}}
+    # a window layer (4 sinks + 256 exact tokens per row): xdecode_tma with each row's merge, L2 flushed
     LW, qw = layers[QUANT_LAYERS], qs[QUANT_LAYERS]
     _, wdur = kernel_roofline(kv800, torch, dev, LW, qw, c32, s32)
     window = {"bytes": LW.algo_bytes(), "us": round(wdur * 1e6, 1),
               "achieved_gbs": round(LW.algo_bytes() / wdur / 1e9, 1), "frac": round(LW.algo_bytes() / wdur / 1e9 / hbm, 4),
-              "kernel": "xdecode_mma with each row's merge, one window layer, L2 flushed"}
+              "kernel": "xdecode_tma (one warp per row, split and head) with the merges, one window layer, L2 flushed"}
 
     # ---- end to end through the public API with host buffers
     e2e = None

@@ -12,6 +12,7 @@
 #include "kv800_common.cuh"
 #include "qdecode_mma.cuh"
 #include "xdecode_mma.cuh"
+#include "xdecode_tma.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -116,8 +117,9 @@ int check_paged(const kv800_paged* P, const char* who) {
 }
 
 // Workspace plan of kv800_decode.  spb > 0: grid splits of spb sub-blocks (ns per row, the reference's sizing);
-// spb <= 0: persistent, G0 CTAs over the flattened sub-block list.  Layout: status word | per-row arrival counters
-// int32 [B] (from byte 256; cleared with the status word before every decode) | prefix[B + 1] (persistent) |
+// spb <= 0: persistent, G0 CTAs over the flattened sub-block list.  Layout: status word | arrival counters int32
+// [B][4] (from byte 256: per (row, head) for the tensor-map form of the exact partials, per row (the first B) for the
+// gather form; cleared with the status word before every decode) | prefix[B + 1] (persistent) |
 // MO, LO [nslots][16] | AO [nslots][16][128], each 256-byte aligned.
 struct Plan {
     bool persistent;
@@ -134,7 +136,7 @@ Plan make_plan(int64_t B, int64_t nqmax, int64_t win, int64_t spb) {
     p.G0 = p.persistent ? persistent_ctas() : 0;
     p.nslots = p.persistent ? p.G0 + B + B * NX_DEFAULT : B * (p.ns + NX_DEFAULT);
     p.cnt_off = 256;
-    p.prefix_off = up256(p.cnt_off + 4 * B);
+    p.prefix_off = up256(p.cnt_off + 4 * HEADS * B);
     p.mo_off = up256(p.prefix_off + (p.persistent ? (B + 1) * 8 : 0));
     p.lo_off = up256(p.mo_off + p.nslots * QROWS * 4);
     p.ao_off = up256(p.lo_off + p.nslots * QROWS * 4);
@@ -151,7 +153,7 @@ extern "C" int64_t kv800_decode_workspace_size(int64_t B, int64_t nqmax, int64_t
 // TMA descriptors of the quant pool as rows of 128 bytes: boxes of 64 rows with the 128-byte swizzle (kc rows and
 // vb lines) and boxes of 16 rows without (the scale region).  The pool must start 16-byte aligned; a sub-block at an
 // offset that is not a multiple of 128 is flagged and skipped by the kernel.
-static int make_qmaps(const uint8_t* qpool, int64_t qpool_bytes, QMArgs& qa) {
+static int tensor_map_encoder(PFN_cuTensorMapEncodeTiled& out) {
     static PFN_cuTensorMapEncodeTiled encode = nullptr;
     if (!encode) {
         cudaDriverEntryPointQueryResult qres;
@@ -165,6 +167,14 @@ static int make_qmaps(const uint8_t* qpool, int64_t qpool_bytes, QMArgs& qa) {
         }
         encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
     }
+    out = encode;
+    return KV800_OK;
+}
+
+static int make_qmaps(const uint8_t* qpool, int64_t qpool_bytes, QMArgs& qa) {
+    PFN_cuTensorMapEncodeTiled encode = nullptr;
+    const int rce = tensor_map_encoder(encode);
+    if (rce) return rce;
     const int64_t rows = qpool_bytes / 128;
     if (!qpool || (reinterpret_cast<uintptr_t>(qpool) & 15u) || rows < 16 || rows > 0x7fffffffLL) {
         set_error("quant pool must be 16-byte aligned and hold between 2 KB and 2^31 x 128 bytes");
@@ -225,9 +235,9 @@ static int xdecode_setup() {
 struct LaunchCfg {
     cudaLaunchConfig_t cfg;
     cudaLaunchAttribute attr;
-    LaunchCfg(dim3 grid, size_t smem, cudaStream_t st, bool early) : cfg{}, attr{} {
+    LaunchCfg(dim3 grid, size_t smem, cudaStream_t st, bool early, unsigned threads = 128) : cfg{}, attr{} {
         cfg.gridDim = grid;
-        cfg.blockDim = dim3(128);
+        cfg.blockDim = dim3(threads);
         cfg.dynamicSmemBytes = smem;
         cfg.stream = st;
         attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -237,11 +247,72 @@ struct LaunchCfg {
     }
 };
 
-// early: the exact partials do not read the quantized ones (the row merge waits for them)
-static void launch_xdecode(const XMArgs& xa, dim3 grid, cudaStream_t st, bool early = false) {
-    LaunchCfg lc(grid, XM_SMEM, st, early);
+// Stages of the tensor-map form's ring (one warp per CTA; 31 KB of shared memory, seven CTAs per SM).
+constexpr int XT_S = 3;
+
+static int xtma_setup() {
+    static std::atomic<int> done[MAX_DEV];
+    return set_smem_once(done, "xdecode_tma smem attribute", [] {
+        int rc = cuda_status(cudaFuncSetAttribute(xdecode_tma<true, XT_S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  xt_smem<XT_S>()),
+                             "xdecode_tma smem attribute");
+        if (rc) return rc;
+        return cuda_status(cudaFuncSetAttribute(xdecode_tma<false, XT_S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                xt_smem<XT_S>()),
+                           "xdecode_tma smem attribute");
+    });
+}
+
+// The tensor-map form applies to exact pools in the reference's page layout (K | V rows of 512 bytes per (head, slot),
+// heads a whole number of rows apart, pages of a multiple of 16 slots) with at most 16 sinks; the tensor map is then
+// the pool as rows of 256 bf16.  Other layouts take the gather form.
+static bool xtma_layout(const kv800_paged& P) {
+    const int64_t rows = P.epool_elems / 256;
+    return P.e_ts == 256 && P.e_v == 128 && P.e_hs >= 0 && P.e_hs % 256 == 0 && P.ebs % 16 == 0 &&
+           !(reinterpret_cast<uintptr_t>(P.epool) & 15u) && rows >= 16 && rows + 3 * (P.e_hs / 256) < 0x7fffffffLL &&
+           (!P.sk || P.nsink <= XT_MAX_SINK);
+}
+
+static int make_emap(const kv800_paged& P, CUtensorMap& tm) {
+    PFN_cuTensorMapEncodeTiled encode = nullptr;
+    const int rce = tensor_map_encoder(encode);
+    if (rce) return rce;
+    cuuint64_t dims[2] = {256, (cuuint64_t)(P.epool_elems / 256)};
+    cuuint64_t strides[1] = {512};
+    cuuint32_t box[2] = {64, 16}, es[2] = {1, 1};
+    const CUresult r = encode(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(P.epool), dims, strides,
+                              box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled (exact pool) failed (%d)", (int)r);
+        return KV800_ERR_CUDA;
+    }
+    return KV800_OK;
+}
+
+// Launch the exact partials of B rows x nx splits: the tensor-map form (one warp per (row, split, head)) where the
+// layout allows it, else the gather form (a 4-warp CTA per (row, split)).  early: the exact partials do not read the
+// quantized ones (the row merge waits for them).
+static int launch_xdecode(const XMArgs& xa, int64_t B, int nx, cudaStream_t st, bool early = false) {
+    if (xtma_layout(xa.P)) {
+        int rc = xtma_setup();
+        if (rc) return rc;
+        XTArgs ta{};
+        rc = make_emap(xa.P, ta.tm);
+        if (rc) return rc;
+        ta.x = xa;
+        ta.ehs_rows = xa.P.e_hs / 256;
+        LaunchCfg lc(dim3((unsigned)B, (unsigned)nx, HEADS), xt_smem<XT_S>(), st, early, 32);
+        if (xa.cos_t) cudaLaunchKernelEx(&lc.cfg, xdecode_tma<true, XT_S>, ta);
+        else cudaLaunchKernelEx(&lc.cfg, xdecode_tma<false, XT_S>, ta);
+        return KV800_OK;
+    }
+    const int rc = xdecode_setup();
+    if (rc) return rc;
+    LaunchCfg lc(dim3((unsigned)B, (unsigned)nx), XM_SMEM, st, early);
     if (xa.cos_t) cudaLaunchKernelEx(&lc.cfg, xdecode_mma<true>, xa);
     else cudaLaunchKernelEx(&lc.cfg, xdecode_mma<false>, xa);
+    return KV800_OK;
 }
 
 // Tables: both given (16-byte aligned, npos > 0), or both null when nothing quantized is decoded (no rotation).
@@ -314,7 +385,8 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
     float* ao = reinterpret_cast<float*>(ws + pl.ao_off);
     int* count = reinterpret_cast<int*>(ws + pl.cnt_off);
     if (!pl.persistent) {   // (the persistent pass clears them in its schedule scan)
-        rc = cuda_status(cudaMemsetAsync(status, 0, pl.cnt_off + 4 * B, st), "kv800_decode status / counter reset");
+        rc = cuda_status(cudaMemsetAsync(status, 0, pl.cnt_off + 4 * HEADS * B, st),
+                         "kv800_decode status / counter reset");
         if (rc) return rc;
     }
     if (ev) cudaEventRecord(ev[0], st);
@@ -323,7 +395,7 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
     if (pl.persistent) {
         rc = qdecode_setup();
         if (rc) return rc;
-        qsched_kernel<<<1, 1024, 0, st>>>(P->NQ, P->nqmax, B, prefix, status, (pl.cnt_off + 4 * B) / 4);
+        qsched_kernel<<<1, 1024, 0, st>>>(P->NQ, P->nqmax, B, prefix, status, (pl.cnt_off + 4 * HEADS * B) / 4);
         rc = cuda_status(cudaGetLastError(), "kv800_decode schedule");
         if (rc) return rc;
         QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
@@ -360,13 +432,12 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
         sm.xbase = pl.ns;
         sm.xstride = rowslots;
     }
-    rc = xdecode_setup();
-    if (rc) return rc;
     if (ev) cudaEventRecord(ev[1], st);
     // the exact partials; the last of a row's NX_DEFAULT CTAs to finish also merges the row's partials into out
     XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, sm.xbase, sm.xstride, NX_DEFAULT, SCALE, status, count, sm, out};
     // early behind a persistent quantized pass (untimed calls): the exact partials fill the SMs its CTAs leave
-    launch_xdecode(xa, dim3((unsigned)B, (unsigned)NX_DEFAULT), st, pl.persistent && !ev);
+    rc = launch_xdecode(xa, B, NX_DEFAULT, st, pl.persistent && !ev);
+    if (rc) return rc;
     rc = cuda_status(cudaGetLastError(), "kv800_decode xdecode");
     if (ev) cudaEventRecord(ev[2], st);
     if (ev) cudaEventRecord(ev[3], st);
@@ -456,10 +527,9 @@ extern "C" int kv800_xdecode(const uint16_t* q, const kv800_paged* P, const uint
         set_error("kv800_xdecode: B %lld above the limit", (long long)B);
         return KV800_ERR_RANGE;
     }
-    int rcx = xdecode_setup();
-    if (rcx) return rcx;
     XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, ns, ns + 1, 1, scale, status, nullptr, SlotMap{}, nullptr};
-    launch_xdecode(xa, dim3((unsigned)B, 1), as_stream(stream));
+    const int rcx = launch_xdecode(xa, B, 1, as_stream(stream));
+    if (rcx) return rcx;
     return cuda_status(cudaGetLastError(), "kv800_xdecode launch");
 }
 

@@ -102,11 +102,204 @@ __device__ __forceinline__ void rope_frag(uint32_t& k0, uint32_t& k2, uint32_t c
 // smem byte offset of (row r, 16-byte chunk c) in a [16 rows][272 B] tile
 __device__ __forceinline__ int xm_off(int r, int c) { return r * XM_ROW + (c << 4); }
 
+// Shared-memory addressing of one head's 16 K and 16 V rows of a tile: the bulk-copy gather's rows at the 272-byte
+// pitch, K and V in separate blocks.
+struct PitchRows {
+    uint32_t kb, vb;
+    __device__ __forceinline__ uint32_t k(int r, int c) const { return kb + xm_off(r, c); }
+    __device__ __forceinline__ uint32_t v(int r, int c) const { return vb + xm_off(r, c); }
+};
+
+// Online-softmax state of one warp (one kv head, its 4 query rows in MMA columns 0..3).
+struct XMState {
+    float m[2], l[2];
+    float acc[8][4];
+    __device__ __forceinline__ void init() {
+        m[0] = m[1] = -1e30f;
+        l[0] = l[1] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) acc[i][k] = 0.f;
+    }
+};
+
+// One 16-token tile of one head (warp): QK on the tensor cores with the in-register RoPE of dims (d, d + 64), d < 32,
+// the masked online softmax (slot s takes part iff bit s of vmask is set) and PV with P split into bf16 hi + lo.
+// cs / sn: the tile's cos / sin rows (16 x 64 B); rows: where the tile's K / V rows sit in shared memory.
+template <bool ROPE, class Rows>
+__device__ __forceinline__ void xm_tile(const Rows& rw, const uint32_t* cs, const uint32_t* sn, const uint32_t (&bq)[8][2],
+                                        uint32_t vmask, float scale, XMState& S, int lane) {
+    const int g = lane >> 2, tig = lane & 3, mi = lane >> 3, ri = lane & 7;
+    // ---- QK: A fragments of the 8 K-steps (matrices: rows 0-7 / 8-15 x dims +0 / +8)
+    uint32_t A[8][4];
+#pragma unroll
+    for (int ks = 0; ks < 8; ks++) {
+        const int r = (mi & 1) * 8 + ri, c = 2 * ks + (mi >> 1);
+        ldsm_x4(rw.k(r, c), A[ks][0], A[ks][1], A[ks][2], A[ks][3]);
+    }
+    // RoPE on K-steps 0,1 (dims 0..31) with 4,5 (dims 64..95): regs 0 / 2 are token g, 1 / 3 token g + 8;
+    // regs 0 / 1 cover dims 16 ks + 2 tig, regs 2 / 3 dims 16 ks + 8 + 2 tig
+    if (ROPE) {
+#pragma unroll
+        for (int ks = 0; ks < 2; ks++)
+#pragma unroll
+            for (int rg = 0; rg < 4; rg++) {
+                const int tok = g + 8 * (rg & 1);
+                const int d = 16 * ks + 8 * (rg >> 1) + 2 * tig;   // even, < 32
+                rope_frag(A[ks][rg], A[ks + 4][rg], cs[tok * 16 + (d >> 1)], sn[tok * 16 + (d >> 1)]);
+            }
+    }
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < 8; ks++) mma_bf16(sc, A[ks][0], A[ks][1], A[ks][2], A[ks][3], bq[ks][0], bq[ks][1]);
+    // masked slots (past the list, outside the row's range, or without valid rows) get -inf by selection, so
+    // whatever their rows hold never reaches the sums
+    const bool va = (vmask >> g) & 1u, vb = (vmask >> (g + 8)) & 1u;
+    float s2[4];
+    s2[0] = va ? sc[0] * scale : -__int_as_float(0x7f800000);
+    s2[1] = va ? sc[1] * scale : -__int_as_float(0x7f800000);
+    s2[2] = vb ? sc[2] * scale : -__int_as_float(0x7f800000);
+    s2[3] = vb ? sc[3] * scale : -__int_as_float(0x7f800000);
+    // the row maxima are reduced across the 8 lanes of a row only when some score of the warp passes its row's
+    // reference point by more than 2^6
+    float lmx[2];
+    bool need = false;
+#pragma unroll
+    for (int rr = 0; rr < 2; rr++) {
+        lmx[rr] = fmaxf(s2[rr], s2[rr + 2]);
+        need |= lmx[rr] > S.m[rr] + 6.0f;
+    }
+    if (__any_sync(0xffffffffu, need)) {
+        float alpha[2] = {1.f, 1.f};
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            float mx = lmx[rr];
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            if (mx > S.m[rr] + 6.0f) {
+                alpha[rr] = fast_exp2(S.m[rr] - mx);
+                S.m[rr] = mx;
+            }
+        }
+        S.l[0] *= alpha[0];
+        S.l[1] *= alpha[1];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            S.acc[i][0] *= alpha[0];
+            S.acc[i][1] *= alpha[1];
+            S.acc[i][2] *= alpha[0];
+            S.acc[i][3] *= alpha[1];
+        }
+    }
+    float p[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) p[k] = fast_exp2(s2[k] - S.m[k & 1]);
+    S.l[0] += p[0] + p[2];
+    S.l[1] += p[1] + p[3];
+    // ---- PV: B = P^T (hi + lo bf16), A = V^T via ldmatrix.trans
+    const uint32_t ha = pack_bf16(p[0], p[1]), hb = pack_bf16(p[2], p[3]);
+    const uint32_t la = pack_bf16(p[0] - __uint_as_float(ha << 16), p[1] - __uint_as_float(ha & 0xffff0000u));
+    const uint32_t lb = pack_bf16(p[2] - __uint_as_float(hb << 16), p[3] - __uint_as_float(hb & 0xffff0000u));
+    const uint32_t bh0 = transpose8x8(ha), bh1 = transpose8x8(hb);
+    const uint32_t bl0 = transpose8x8(la), bl1 = transpose8x8(lb);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        // matrices: (tokens 0-7, dims +0), (tokens 0-7, dims +8), (tokens 8-15, dims +0), (tokens 8-15, dims +8)
+        const int r = (mi >> 1) * 8 + ri, c = 2 * i + (mi & 1);
+        uint32_t v0, v1, v2, v3;
+        ldsm_x4_t(rw.v(r, c), v0, v1, v2, v3);
+        mma_bf16(S.acc[i], v0, v1, v2, v3, bh0, bh1);
+        mma_bf16(S.acc[i], v0, v1, v2, v3, bl0, bl1);
+    }
+}
+
+// q B fragments of warp h (standard dims layout): b0 = q[g][16 ks + 2 tig ..], b1 = q[g][16 ks + 8 + 2 tig ..]
+__device__ __forceinline__ void xm_load_q(const uint16_t* q, int b, int h, int lane, uint32_t (&bq)[8][2]) {
+    const int g = lane >> 2, tig = lane & 3;
+    const uint16_t* qr = q + ((int64_t)b * QROWS + h * 4 + (g & 3)) * DIM;
+#pragma unroll
+    for (int ks = 0; ks < 8; ks++) {
+        const uint32_t v0 = *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 2 * tig);
+        const uint32_t v1 = *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 8 + 2 * tig);
+        bq[ks][0] = (g < 4) ? v0 : 0u;
+        bq[ks][1] = (g < 4) ? v1 : 0u;
+    }
+}
+
+// The partial of split e of row b (slot xbase + b xstride + e) for warp h's query rows: rows r = 2 tig, 2 tig + 1
+// (valid for tig < 2); acc[i] rows d = 16 i + g, 16 i + g + 8.
+__device__ __forceinline__ void xm_store_partial(const XMArgs& a, const XMState& S, int b, int e, int h, int lane) {
+    const int g = lane >> 2, tig = lane & 3;
+    float l[2];
+#pragma unroll
+    for (int rr = 0; rr < 2; rr++) {
+        float x = S.l[rr];
+        x += __shfl_xor_sync(0xffffffffu, x, 4);
+        x += __shfl_xor_sync(0xffffffffu, x, 8);
+        x += __shfl_xor_sync(0xffffffffu, x, 16);
+        l[rr] = x;
+    }
+    if (tig < 2) {
+        const int64_t slot = a.xbase + (int64_t)b * a.xstride + e;
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            const int64_t row = slot * QROWS + h * 4 + 2 * tig + rr;
+            if (g == 0) {
+                a.mo[row] = S.m[rr];
+                a.lo[row] = l[rr];
+            }
+            float* o = a.ao + row * DIM;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                o[16 * i + g] = S.acc[i][rr];
+                o[16 * i + g + 8] = S.acc[i][rr + 2];
+            }
+        }
+    }
+}
+
+// Partial and merge of a 4-warp CTA (warp h = head h): with arrival counters (one per row, target nx) the last CTA of
+// row b to arrive merges the row (warp h: query rows 4 h .. 4 h + 3).  Every thread of the CTA calls it.
+__device__ __forceinline__ void xm_finish(const XMArgs& a, const XMState& S, int b, int e, int h, int lane) {
+    xm_store_partial(a, S, b, e, h, lane);
+    if (a.count) {
+        __shared__ int last;
+        __threadfence();
+        __syncthreads();
+        if (h == 0 && lane == 0) last = atomicAdd(a.count + b, 1) == a.nx - 1;
+        __syncthreads();
+        if (last) {   // (launched early behind the quantized-partial kernel: the merge waits for it after the exact
+                      // group)
+            __threadfence();
+            combine_head(a.mo, a.lo, a.ao, a.sm, a.out, b, h, lane, true);
+        }
+    }
+}
+
+// Partial and merge of a one-warp CTA (row b, split e, head h): with arrival counters (one per (row, head), at
+// b * 4 + h, target nx) the last warp of (b, h) to arrive merges head h's query rows of row b.
+__device__ __forceinline__ void xm_finish_head(const XMArgs& a, const XMState& S, int b, int e, int h, int lane) {
+    xm_store_partial(a, S, b, e, h, lane);
+    if (a.count) {
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(a.count + (int64_t)b * HEADS + h, 1) == a.nx - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            __threadfence();
+            combine_head(a.mo, a.lo, a.ao, a.sm, a.out, b, h, lane, true);
+        }
+    }
+}
+
 template <bool ROPE>
 __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];   // the same declaration as qdecode_mma's (one symbol per unit)
     const int b = blockIdx.x, e = blockIdx.y, tid = threadIdx.x;
-    const int h = tid >> 5, lane = tid & 31, g = lane >> 2, tig = lane & 3;
+    const int h = tid >> 5, lane = tid & 31;
     const kv800_paged& P = a.P;
 
     // ---- this split's token list: [s0, cnt) sinks, then exact positions lo_e + [x0, x1)
@@ -203,18 +396,8 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
         else if (tdst) zero_row(tdst, 64);
     };
 
-    // ---- q B fragments (standard dims layout): b0 = q[g][16 ks + 2 tig ..], b1 = q[g][16 ks + 8 + 2 tig ..]
     uint32_t bq[8][2];
-    {
-        const uint16_t* qr = a.q + ((int64_t)b * QROWS + h * 4 + (g & 3)) * DIM;
-#pragma unroll
-        for (int ks = 0; ks < 8; ks++) {
-            const uint32_t v0 = *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 2 * tig);
-            const uint32_t v1 = *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 8 + 2 * tig);
-            bq[ks][0] = (g < 4) ? v0 : 0u;
-            bq[ks][1] = (g < 4) ? v1 : 0u;
-        }
-    }
+    xm_load_q(a.q, b, h, lane, bq);
     if (tid == 0) {
         mbar_init_count(bar0, 128);
         mbar_init_count(bar0 + 8, 128);
@@ -226,150 +409,27 @@ __global__ void __launch_bounds__(128, 3) xdecode_mma(XMArgs a) {
     uint32_t phase = 0;      // bit s: parity of the next phase of stage s's mbarrier
     int timeouts = 0;
 
-    float m[2] = {-1e30f, -1e30f}, l_part[2] = {0.f, 0.f};
-    float acc[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; i++)
-#pragma unroll
-        for (int k = 0; k < 4; k++) acc[i][k] = 0.f;
-
-    // ldmatrix lane roles: matrix mi = lane / 8, row-in-matrix ri = lane % 8
-    const int mi = lane >> 3, ri = lane & 7;
+    XMState S;
+    S.init();
     for (int it = 0; it < ntiles; it++) {
         const int st = it & 1;
         if (!mbar_wait(bar0 + 8 * st, (phase >> st) & 1u)) timeouts++;
         phase ^= 1u << st;
         __syncthreads();   // the zero-filled rows of other threads
         const uint8_t* base = smem + st * XM_STAGE;
-        const uint32_t kb = smem_u32(base + h * XM_HEAD_BYTES);
-        const uint32_t vb = smem_u32(base + XM_KV_BYTES + h * XM_HEAD_BYTES);
+        const PitchRows rw{smem_u32(base + h * XM_HEAD_BYTES), smem_u32(base + XM_KV_BYTES + h * XM_HEAD_BYTES)};
         const uint32_t* cs = reinterpret_cast<const uint32_t*>(base + 2 * XM_KV_BYTES);
         const uint32_t* sn = reinterpret_cast<const uint32_t*>(base + 2 * XM_KV_BYTES + XM_CS_BYTES);
-        // ---- QK: A fragments of the 8 K-steps (matrices: rows 0-7 / 8-15 x dims +0 / +8)
-        uint32_t A[8][4];
-#pragma unroll
-        for (int ks = 0; ks < 8; ks++) {
-            const int r = (mi & 1) * 8 + ri, c = 2 * ks + (mi >> 1);
-            ldsm_x4(kb + xm_off(r, c), A[ks][0], A[ks][1], A[ks][2], A[ks][3]);
-        }
-        // RoPE on K-steps 0,1 (dims 0..31) with 4,5 (dims 64..95): regs 0 / 2 are token g, 1 / 3 token g + 8;
-        // regs 0 / 1 cover dims 16 ks + 2 tig, regs 2 / 3 dims 16 ks + 8 + 2 tig
-        if (ROPE) {
-#pragma unroll
-            for (int ks = 0; ks < 2; ks++)
-#pragma unroll
-                for (int rg = 0; rg < 4; rg++) {
-                    const int tok = g + 8 * (rg & 1);
-                    const int d = 16 * ks + 8 * (rg >> 1) + 2 * tig;   // even, < 32
-                    rope_frag(A[ks][rg], A[ks + 4][rg], cs[tok * 16 + (d >> 1)], sn[tok * 16 + (d >> 1)]);
-                }
-        }
-        float sc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int ks = 0; ks < 8; ks++) mma_bf16(sc, A[ks][0], A[ks][1], A[ks][2], A[ks][3], bq[ks][0], bq[ks][1]);
-        // mask tokens past the list end or without valid rows (zero-filled rows still give finite scores, but the
-        // list end is the only place rows are missing when the tables are consistent)
-        const int64_t t_a = (int64_t)it * XM_TILE + g, t_b = t_a + 8;
-        float s2[4];
-        s2[0] = (t_a < total) ? sc[0] * a.scale : -__int_as_float(0x7f800000);
-        s2[1] = (t_a < total) ? sc[1] * a.scale : -__int_as_float(0x7f800000);
-        s2[2] = (t_b < total) ? sc[2] * a.scale : -__int_as_float(0x7f800000);
-        s2[3] = (t_b < total) ? sc[3] * a.scale : -__int_as_float(0x7f800000);
-        // the row maxima are reduced across the 8 lanes of a row only when some score of the warp passes its row's
-        // reference point by more than 2^6
-        float lmx[2];
-        bool need = false;
-#pragma unroll
-        for (int rr = 0; rr < 2; rr++) {
-            lmx[rr] = fmaxf(s2[rr], s2[rr + 2]);
-            need |= lmx[rr] > m[rr] + 6.0f;
-        }
-        if (__any_sync(0xffffffffu, need)) {
-            float alpha[2] = {1.f, 1.f};
-#pragma unroll
-            for (int rr = 0; rr < 2; rr++) {
-                float mx = lmx[rr];
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                if (mx > m[rr] + 6.0f) {
-                    alpha[rr] = fast_exp2(m[rr] - mx);
-                    m[rr] = mx;
-                }
-            }
-            l_part[0] *= alpha[0];
-            l_part[1] *= alpha[1];
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                acc[i][0] *= alpha[0];
-                acc[i][1] *= alpha[1];
-                acc[i][2] *= alpha[0];
-                acc[i][3] *= alpha[1];
-            }
-        }
-        float p[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) p[k] = fast_exp2(s2[k] - m[k & 1]);
-        l_part[0] += p[0] + p[2];
-        l_part[1] += p[1] + p[3];
-        // ---- PV: B = P^T (hi + lo bf16), A = V^T via ldmatrix.trans
-        const uint32_t ha = pack_bf16(p[0], p[1]), hb = pack_bf16(p[2], p[3]);
-        const uint32_t la = pack_bf16(p[0] - __uint_as_float(ha << 16), p[1] - __uint_as_float(ha & 0xffff0000u));
-        const uint32_t lb = pack_bf16(p[2] - __uint_as_float(hb << 16), p[3] - __uint_as_float(hb & 0xffff0000u));
-        const uint32_t bh0 = transpose8x8(ha), bh1 = transpose8x8(hb);
-        const uint32_t bl0 = transpose8x8(la), bl1 = transpose8x8(lb);
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            // matrices: (tokens 0-7, dims +0), (tokens 0-7, dims +8), (tokens 8-15, dims +0), (tokens 8-15, dims +8)
-            const int r = (mi >> 1) * 8 + ri, c = 2 * i + (mi & 1);
-            uint32_t v0, v1, v2, v3;
-            ldsm_x4_t(vb + xm_off(r, c), v0, v1, v2, v3);
-            mma_bf16(acc[i], v0, v1, v2, v3, bh0, bh1);
-            mma_bf16(acc[i], v0, v1, v2, v3, bl0, bl1);
-        }
+        // slots past the list end are masked (zero-filled rows still give finite scores, but the list end is the
+        // only place rows are missing when the tables are consistent)
+        const int64_t left = total - (int64_t)it * XM_TILE;
+        const uint32_t vmask = left >= XM_TILE ? 0xffffu : ((1u << left) - 1u);
+        xm_tile<ROPE>(rw, cs, sn, bq, vmask, a.scale, S, lane);
         __syncthreads();
         if (it + 2 < ntiles) issue(it + 2, st);
     }
     if (timeouts && tid == 0) flag(a.status, ST_TIMEOUT);
-    // ---- partial: rows r = 2 tig, 2 tig + 1 (valid for tig < 2); acc[i] rows d = 16 i + g, 16 i + g + 8
-    float l[2];
-#pragma unroll
-    for (int rr = 0; rr < 2; rr++) {
-        float x = l_part[rr];
-        x += __shfl_xor_sync(0xffffffffu, x, 4);
-        x += __shfl_xor_sync(0xffffffffu, x, 8);
-        x += __shfl_xor_sync(0xffffffffu, x, 16);
-        l[rr] = x;
-    }
-    if (tig < 2) {
-        const int64_t slot = a.xbase + (int64_t)b * a.xstride + e;
-#pragma unroll
-        for (int rr = 0; rr < 2; rr++) {
-            const int64_t row = slot * QROWS + h * 4 + 2 * tig + rr;
-            if (g == 0) {
-                a.mo[row] = m[rr];
-                a.lo[row] = l[rr];
-            }
-            float* o = a.ao + row * DIM;
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                o[16 * i + g] = acc[i][rr];
-                o[16 * i + g + 8] = acc[i][rr + 2];
-            }
-        }
-    }
-    if (a.count) {   // the last CTA of row b to arrive merges the row (warp h: query rows 4 h .. 4 h + 3)
-        __shared__ int last;
-        __threadfence();
-        __syncthreads();
-        if (tid == 0) last = atomicAdd(a.count + b, 1) == a.nx - 1;
-        __syncthreads();
-        if (last) {   // (launched early behind the quantized-partial kernel: the merge waits for it after the exact
-                      // group)
-            __threadfence();
-            combine_head(a.mo, a.lo, a.ao, a.sm, a.out, b, h, lane, true);
-        }
-    }
+    xm_finish(a, S, b, e, h, lane);
 }
 
 }  // namespace kv800

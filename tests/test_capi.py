@@ -109,7 +109,7 @@ def _plan_bytes(B, nqmax, win, spb, G0=444):
     persistent = spb <= 0 and nq > 0
     ns = 0 if (nq == 0 or persistent) else -(-nq // spb)
     nslots = (G0 + B + 4 * B) if persistent else B * (ns + 4)
-    prefix = up(256 + 4 * B)                       # status word | per-row arrival counters
+    prefix = up(256 + 16 * B)                      # status word | arrival counters per (row, head)
     mo = up(prefix + ((B + 1) * 8 if persistent else 0))
     lo = up(mo + nslots * 64)
     ao = up(lo + nslots * 64)
@@ -119,7 +119,7 @@ def _plan_bytes(B, nqmax, win, spb, G0=444):
 @pytest.mark.parametrize("B,nqmax,win,spb", [(64, 127, 0, 0), (4, 7, 0, 0), (64, 0, 256, 0), (2048, 127, 0, 0),
                                              (2, 19, 0, 3), (64, 127, 0, 7)])
 def test_workspace_size(B, nqmax, win, spb):
-    """Workspace plan: status word, per-row arrival counters, schedule prefix (persistent), MO / LO / AO partials
+    """Workspace plan: status word, arrival counters, schedule prefix (persistent), MO / LO / AO partials
     (no GPU: the persistent CTA count falls back to 3 x 148 when no device answers)."""
     L = _lib.lib()
     assert L.kv800_decode_workspace_size(B, nqmax, win, spb) == _plan_bytes(B, nqmax, win, spb)

@@ -15,9 +15,11 @@ DEV = "cuda"
 EBS = 64
 
 
-def build(lengths, win, seed, distinct=None):
+def build(lengths, win, seed, distinct=None, ebs=EBS, pitch=256):
     """Host pools for rows of `lengths`; `distinct` = quantize only that many different sub-blocks and scatter them
-    at random over the rows' tables (the quantized part need not match the exact pages)."""
+    at random over the rows' tables (the quantized part need not match the exact pages).  Exact pages hold `ebs`
+    slots per head with rows of `pitch` elements (K at 0, V at 128; 256 is the reference's layout)."""
+    EBS = ebs
     rs = np.random.RandomState(seed)
     B = len(lengths)
     nqs = [0 if win else max(0, n - 128) // 256 for n in lengths]
@@ -29,7 +31,7 @@ def build(lengths, win, seed, distinct=None):
     eoff = np.zeros((B, maxpg), np.int64)
     npages = sum(n // EBS + 1 for n in lengths) + 3
     pages = rs.permutation(npages)
-    epool = np.zeros((npages, 4, EBS, 256), np.uint16)
+    epool = np.zeros((npages, 4, EBS, pitch), np.uint16)
     # token data: every position when the sub-blocks are built from it, else only what the decode reads (the exact
     # positions [256 nq, n) and the 4 sink positions); other positions stay zero
     K_all, V_all = [], []
@@ -63,13 +65,13 @@ def build(lengths, win, seed, distinct=None):
     pi = 0
     for b, n in enumerate(lengths):
         npg = n // EBS + 1
-        eoff[b, :npg] = pages[pi:pi + npg] * 4 * EBS * 256
+        eoff[b, :npg] = pages[pi:pi + npg] * 4 * EBS * pitch
         pi += npg
         if n:
             t = np.arange(n)
-            pg = eoff[b, t // EBS] // (4 * EBS * 256)
+            pg = eoff[b, t // EBS] // (4 * EBS * pitch)
             epool[pg, :, t % EBS, :128] = K_all[b]
-            epool[pg, :, t % EBS, 128:] = V_all[b]
+            epool[pg, :, t % EBS, 128:256] = V_all[b]
     sk = np.zeros((B, 4, 4, 128), np.uint16)
     for b, n in enumerate(lengths):
         m = min(4, n)
@@ -79,7 +81,7 @@ def build(lengths, win, seed, distinct=None):
         m = min(4, n)
         sv[b, :m] = V_all[b][:m]
     q = I.f32_to_bf16(2 * rs.standard_normal((B, 16, 128)).astype(np.float32))
-    P = dict(qpool=qpool, boff=boff, epool=epool, eoff=eoff, ebs=EBS, e_hs=EBS * 256, e_ts=256, e_v=128,
+    P = dict(qpool=qpool, boff=boff, epool=epool, eoff=eoff, ebs=EBS, e_hs=EBS * pitch, e_ts=pitch, e_v=128,
              sk=sk if win else None, sv=sv if win else None, skoff=np.arange(B, dtype=np.int64) * 2048,
              svoff=np.arange(B, dtype=np.int64) * 2048, N=np.array(lengths, np.int32), NQ=np.array(nqs, np.int32),
              nqmax=max(nqs), win=win)
@@ -109,6 +111,23 @@ def test_ragged_vs_oracle(win, spb):
     got = nb(out)
     assert_parity_ulp(got, ref, f"ragged win={win} spb={spb}")
     assert np.all(got[0] == 0), "the empty row must decode to zeros"
+
+
+@pytest.mark.parametrize("ebs,pitch", [(16, 256), (128, 256), (24, 256), (64, 384)])
+@pytest.mark.parametrize("win", [0, 256])
+def test_exact_page_layouts(ebs, pitch, win, monkeypatch):
+    """Both forms of the exact partials against the oracle: pages of a multiple of 16 slots with 512-byte K | V rows
+    (the reference's layout) take the tensor-map form, other page sizes and padded rows the gather form.  Windows
+    start at positions that are not multiples of 16, so first and last tiles are partly masked.  The status word
+    must stay 0 (no spurious range flags)."""
+    from lfm3_kv800 import kv800
+    monkeypatch.setattr(kv800, "_CHECK", True)
+    P, q = build(LENGTHS, win, seed=31 + ebs + pitch + win, ebs=ebs, pitch=pitch)
+    cs, sn = I.rope_tables(5200)
+    for spb in (None, 3):
+        got = nb(kv800.decode(to_dev(kv800, P), tb(q, DEV), tb(cs, DEV), tb(sn, DEV), spb=spb))
+        assert_parity_ulp(got, O.decode(P, q, cs, sn), f"ebs={ebs} pitch={pitch} win={win} spb={spb}")
+        assert np.all(got[0] == 0)
 
 
 def test_persistent_many_rows():
