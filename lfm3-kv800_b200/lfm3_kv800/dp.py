@@ -51,10 +51,13 @@ def gather_rows(out, rows, total, device=None):
     pad[:len(rows)] = out
     idx = torch.full((m,), -1, dtype=torch.int64, device=device)
     idx[:len(rows)] = torch.as_tensor(rows, dtype=torch.int64, device=device)
-    outs = [torch.zeros_like(pad) for _ in range(world)]
+    # the rows travel as their bytes: NCCL moves no int16 / uint16 tensors, and a byte copy is exact for any dtype
+    raw = pad.contiguous().view(torch.uint8)
+    outs = [torch.zeros_like(raw) for _ in range(world)]
     idxs = [torch.zeros_like(idx) for _ in range(world)]
-    dist.all_gather(outs, pad)
+    dist.all_gather(outs, raw)
     dist.all_gather(idxs, idx)
+    outs = [o.view(out.dtype) for o in outs]
     if dist.get_rank() != 0:
         return None
     full = torch.zeros((total,) + tuple(out.shape[1:]), dtype=out.dtype, device=device)

@@ -50,12 +50,24 @@ def _worker(rank, world, port, result):
         rows = D.shard_rows(lengths, world, rank)
         sub = dict(P, boff=P["boff"][rows], eoff=P["eoff"][rows], N=P["N"][rows], NQ=P["NQ"][rows],
                    skoff=P["skoff"][rows], svoff=P["svoff"][rows])
-        out = torch.from_numpy(O.decode(sub, q[rows], cs, sn, nthreads=2).astype(np.int32))   # gloo: no int16
-        full = D.gather_rows(out, rows, len(lengths))
+        # the bf16 bits as int16, the dtype the bench gathers; every collective of gather_rows must use a dtype
+        # NCCL moves (it has no int16 / uint16)
+        out = torch.from_numpy(O.decode(sub, q[rows], cs, sn, nthreads=2).view(np.int16))
+        seen = []
+        real = dist.all_gather
+        def recording(outs, t, *args, **kw):
+            seen.append(t.dtype)
+            return real(outs, t, *args, **kw)
+        dist.all_gather = recording
+        try:
+            full = D.gather_rows(out, rows, len(lengths))
+        finally:
+            dist.all_gather = real
         slowest = D.max_over_ranks(1.0 + rank)
         if rank == 0:
-            ref = O.decode(P, q, cs, sn, nthreads=2).astype(np.int32)
-            result["equal"] = bool(np.array_equal(full.numpy(), ref))
+            ref = O.decode(P, q, cs, sn, nthreads=2).view(np.int16)
+            result["equal"] = bool(full.dtype == torch.int16 and np.array_equal(full.numpy(), ref))
+            result["dtypes"] = sorted({str(d) for d in seen})
             result["max"] = slowest
             result["rows0"] = rows
     finally:
@@ -75,5 +87,6 @@ def test_sharded_decode_gathers_to_full_batch():
             p.join(240)
         assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
         assert result["equal"], "gathered shards differ from the full-batch decode"
+        assert set(result["dtypes"]) <= {"torch.uint8", "torch.int64"}, result["dtypes"]
         assert result["max"] == 2.0
         assert 0 < len(result["rows0"]) < 8
