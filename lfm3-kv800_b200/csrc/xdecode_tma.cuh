@@ -13,6 +13,9 @@
 //   copies   lane 0 issues, per tile, 4 TMA boxes (the head's 4 quarters, 16 rows x 128 bytes, 128-byte swizzle) and
 //            the tile's cos / sin rows (one bulk copy each) into an S-stage ring, one mbarrier per stage.  Rows past
 //            the pool read as zeros (the tensor map's bounds); a tile whose page fails the checks gets no copies.
+//            A page whose offset is not a multiple of 256 elements (but keeps the rows 16-byte aligned, all the
+//            gather form needs) is not on the tensor's row grid: the warp loads that tile's rows with plain 16-byte
+//            loads instead, so every page table the gather form accepts gives the same result here.
 //   compute  xm_tile on the swizzled rows: 16-byte unit u of row r of a quarter sits at unit u ^ (r & 7), so the 8
 //            rows an ldmatrix reads fall in 8 different bank groups.  V rows of masked slots are zeroed first (their
 //            scores are masked by selection, but 0 x NaN would reach the PV sums).
@@ -58,9 +61,10 @@ struct SwzRows {
     __device__ __forceinline__ uint32_t v(int r, int c) const { return k(r, c) + 2 * XT_BOX; }
 };
 
-// Row (of the 2-D pool) of head h, slot p0 % ebs of the page holding position p0, or -1 when the page table entry,
-// the page offset or the rows used (slots [lo, hi) of the tile) fail the checks (status bit set).  Positions and
-// page sizes are below 2^31 (N is int32, ebs checked by the host).
+// Element offset of the row of head h, slot p0 % ebs of the page holding position p0 (a multiple of 256 when the page
+// lies on the tensor's row grid), or -1 when the page table entry, the rows' 16-byte alignment or the rows used
+// (slots [lo, hi) of the tile) fail the checks (status bit set).  Positions and page sizes are below 2^31 (N is
+// int32, ebs checked by the host).
 __device__ __forceinline__ int64_t xt_page_row(const kv800_paged& P, int64_t ehs_rows, int b, int h, uint32_t p0,
                                                int lo, int hi, int* status) {
     const uint32_t eb = (uint32_t)P.ebs, pg = p0 / eb, sl = p0 - pg * eb;
@@ -70,11 +74,24 @@ __device__ __forceinline__ int64_t xt_page_row(const kv800_paged& P, int64_t ehs
     }
     const int64_t off = P.eoff[(int64_t)b * P.eoff_stride + pg] + (int64_t)h * ehs_rows * 256;
     // the rows of the slots used lie inside the pool
-    if (off < 0 || (off & 255) || off + ((int64_t)sl + hi) * 256 > P.epool_elems || hi <= lo) {
+    if (off < 0 || (off & 7) || off + ((int64_t)sl + hi) * 256 > P.epool_elems || hi <= lo) {
         flag(status, ST_EPOOL);
         return -1;
     }
-    return (off >> 8) + sl;
+    return off + (int64_t)sl * 256;
+}
+
+// The K | V rows of a tile whose page is off the tensor's row grid, by plain 16-byte loads into the swizzled layout:
+// slots [lo, hi) from src (slot s at src + 256 s), zeros elsewhere.  Kept out of line: it is the rare path, and
+// inlined it would raise the register count of the whole loop.
+__device__ __noinline__ void xt_fill_rows(uint8_t* base, const uint16_t* src, int lo, int hi, int lane) {
+    for (int idx = lane; idx < 16 * 32; idx += 32) {
+        const int s = idx >> 5, u = idx & 31;   // 512-byte K | V row: units 0..15 K, 16..31 V
+        uint4 val = make_uint4(0u, 0u, 0u, 0u);
+        if (s >= lo && s < hi) val = *reinterpret_cast<const uint4*>(src + s * 256 + 8 * u);
+        *reinterpret_cast<uint4*>(base + (u >> 3) * XT_BOX + s * 128 + (((u & 7) ^ (s & 7)) << 4)) = val;
+    }
+    __syncwarp();
 }
 
 template <bool ROPE, int S>
@@ -85,7 +102,7 @@ __global__ void __launch_bounds__(32) xdecode_tma(const __grid_constant__ XTArgs
     const int b = blockIdx.x, e = blockIdx.y, h = blockIdx.z, lane = threadIdx.x;
     uint8_t* ring = smem + ((1024 - (smem_u32(smem) & 1023)) & 1023);   // stages 1024-aligned for the swizzle
     int64_t* tab = reinterpret_cast<int64_t*>(ring + S * XT_STAGE);   // page rows of the first XT_TAB tiles
-    int64_t* srow = tab + XT_TAB;                                       // page row of the tile in stage s
+    int64_t* srow = tab + XT_TAB;                                       // row offset of the tile in stage s
     const uint32_t bar0 = smem_u32(srow + S);                           // mbarrier of stage s at bar0 + 8 s
 
     uint32_t bq[8][2];
@@ -126,15 +143,17 @@ __global__ void __launch_bounds__(32) xdecode_tma(const __grid_constant__ XTArgs
         uint8_t* base = ring + st * XT_STAGE;
         const uint32_t bar = bar0 + 8 * st;
         srow[st] = row;   // for the loop: written before the arrive, whose release the phase's waiters acquire
-        uint32_t bytes = row >= 0 ? (uint32_t)XT_KV : 0u;
+        const bool boxes = row >= 0 && !(row & 255);   // on the tensor's row grid (else plain loads in the loop)
+        uint32_t bytes = boxes ? (uint32_t)XT_KV : 0u;
         int nt = 0;   // table rows copied (positions p0 .. p0 + nt - 1 below npos)
         if (ROPE && (int64_t)p0 < a.npos) nt = (int)min((int64_t)16, a.npos - p0);
         bytes += 2u * 64u * (uint32_t)nt;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_arrive_tx(bar, bytes);
-        if (row >= 0) {
+        if (boxes) {
 #pragma unroll
-            for (int qq = 0; qq < 4; qq++) tma2d_xy(smem_u32(base + qq * XT_BOX), &t.tm, 64 * qq, (int)row, bar);
+            for (int qq = 0; qq < 4; qq++)
+                tma2d_xy(smem_u32(base + qq * XT_BOX), &t.tm, 64 * qq, (int)(row >> 8), bar);
         }
         if (nt > 0) {
             bulk_g2s(smem_u32(base + XT_KV), a.cos_t + (int64_t)p0 * 32, 64u * nt, bar);
@@ -200,8 +219,9 @@ __global__ void __launch_bounds__(32) xdecode_tma(const __grid_constant__ XTArgs
             const uint32_t j = t0 + (uint32_t)(it - has_sink);
             int lo, hi;
             slot_range(j, lo, hi);
-            vmask = (srow[st] >= 0 && hi > lo) ? (((hi >= 16) ? 0xffffu : ((1u << hi) - 1u)) & ~((1u << lo) - 1u))
-                                               : 0u;
+            const int64_t row = srow[st];
+            if (row >= 0 && (row & 255)) xt_fill_rows(base, P.epool + row, lo, hi, lane);   // off the row grid
+            vmask = (row >= 0 && hi > lo) ? (((hi >= 16) ? 0xffffu : ((1u << hi) - 1u)) & ~((1u << lo) - 1u)) : 0u;
             if (ROPE && 16 * (int64_t)j + 16 > a.npos) {   // positions without a table row (flagged, as in the gather
                                                            // form)
                 const int64_t ok = a.npos - 16 * (int64_t)j;

@@ -130,6 +130,23 @@ def test_exact_page_layouts(ebs, pitch, win, monkeypatch):
         assert np.all(got[0] == 0)
 
 
+@pytest.mark.parametrize("win", [0, 256])
+def test_exact_pages_off_the_row_grid(win, monkeypatch):
+    """Page offsets that keep every row 16-byte aligned but are not multiples of 256 elements (the pool starts 8
+    elements into its buffer): the reference's strides select the tensor-map form, which loads such tiles with plain
+    loads.  Must meet the bar against the oracle with the status word 0, as the gather form did for them."""
+    from lfm3_kv800 import kv800
+    monkeypatch.setattr(kv800, "_CHECK", True)
+    P, q = build(LENGTHS, win, seed=41 + win)
+    P["epool"] = np.concatenate([np.zeros(8, np.uint16), P["epool"].ravel()])
+    P["eoff"] = P["eoff"] + 8
+    cs, sn = I.rope_tables(5200)
+    for spb in (None, 3):
+        got = nb(kv800.decode(to_dev(kv800, P), tb(q, DEV), tb(cs, DEV), tb(sn, DEV), spb=spb))
+        assert_parity_ulp(got, O.decode(P, q, cs, sn), f"off-grid pages win={win} spb={spb}")
+        assert np.all(got[0] == 0)
+
+
 def test_persistent_many_rows():
     """More rows than persistent CTAs with tiny sub-block lists: every CTA range crosses several rows."""
     from lfm3_kv800 import kv800
