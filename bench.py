@@ -873,7 +873,8 @@ def main():
                 "frac": round(kbytes / kdur / 1e9 / hbm, 4), "traffic": traffic, "peak_source": peak_kind,
                 "kernel": "qdecode_mma (+ its 1-CTA schedule scan)", "bytes_per_launch": kbytes,
                 "launch_us": round(kdur * 1e6, 1),
-                "layer_decode": {"bytes": L0.algo_bytes(), "us": round(ldur * 1e6, 1),
+                "layer_decode": {"bytes": L0.algo_bytes(), "bytes_quantized": kbytes,
+                                 "bytes_exact": L0.algo_bytes() - kbytes, "us": round(ldur * 1e6, 1),
                                  "achieved_gbs": round(L0.algo_bytes() / ldur / 1e9, 1),
                                  "kernels": "qsched + qdecode_mma + xdecode_tma (with the merge of each row's partials)"}}
     # a window layer (4 sinks + 256 exact tokens per row): xdecode_tma with each row's merge, L2 flushed
@@ -943,7 +944,10 @@ def main():
                            "timing": window_summary(wins, a.steps)},
                 "hbm_gbs_step": round(step_bytes * a.steps / t / 1e9, 1),
                 "hbm_frac_step": round(step_bytes * a.steps / t / 1e9 / hbm, 4),
-                "bytes_per_step_per_gpu": step_bytes, "roofline": roofline, "window_layer": window, "parity": parity,
+                "bytes_per_step_per_gpu": step_bytes,
+                "bytes_per_step_split": {"quantized": sum(L.B * L.nq * SUB for L in layers),
+                                         "exact": step_bytes - sum(L.B * L.nq * SUB for L in layers)},
+                "roofline": roofline, "window_layer": window, "parity": parity,
                 "cpu_baseline": cpu,
                 "cpu_baseline_port": cpu_port, "e2e": e2e,
                 "gpu_launches": launches_per_step * a.steps, "clocks": clocks, "config1": cfg1, "flush": flush,
