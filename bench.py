@@ -825,6 +825,7 @@ def main():
     layers, qs, c32, s32 = build_workload(kv800, torch, dev, rank, B=a.seqs, n=a.ctx)
     torch.cuda.synchronize()
     step_bytes = sum(L.algo_bytes() for L in layers)
+    quant_bytes = sum(L.B * L.nq * SUB for L in layers)   # the sub-block part; the rest is exact tokens and sinks
     hbm, peak_kind = peaks()
 
     def step():
@@ -945,8 +946,7 @@ def main():
                 "hbm_gbs_step": round(step_bytes * a.steps / t / 1e9, 1),
                 "hbm_frac_step": round(step_bytes * a.steps / t / 1e9 / hbm, 4),
                 "bytes_per_step_per_gpu": step_bytes,
-                "bytes_per_step_split": {"quantized": sum(L.B * L.nq * SUB for L in layers),
-                                         "exact": step_bytes - sum(L.B * L.nq * SUB for L in layers)},
+                "bytes_per_step_split": {"quantized": quant_bytes, "exact": step_bytes - quant_bytes},
                 "roofline": roofline, "window_layer": window, "parity": parity,
                 "cpu_baseline": cpu,
                 "cpu_baseline_port": cpu_port, "e2e": e2e,
