@@ -231,8 +231,8 @@ KV800_API int kv800_decode_noalloc_status(int* host_value, void* stream);
 /*
  * kv800_decode_timed -- has no counterpart in the reference: kv800_decode with CUDA events around its phases, for
  * benchmarks.  Blocks until the decode is done and writes ms[0] = the quantized partials (schedule + qdecode_mma),
- * ms[1] = the exact partials (xdecode_mma) together with the merge of each row's partials, which the row's last
- * exact-partial CTA performs, ms[2] = the gap after it (about zero), in milliseconds of device time.  A phase with no work
+ * ms[1] = the exact partials together with the merge of each row's partials, which the last exact-partial CTA of
+ * each row (or (row, head)) performs, ms[2] = the gap after it (about zero), in milliseconds of device time.  A phase with no work
  * reports the gap between its two events (about zero).
  */
 KV800_API int kv800_decode_timed(const kv800_paged* P, const uint16_t* q, const uint16_t* cos_t,

@@ -1,6 +1,7 @@
 // Log-sum-exp merge of a row's split partials, with the in-register Hadamard for the quantized part (kv800.py:231-236).
 // One warp merges the 4 query rows of one kv head; the standalone combine kernel runs it for every (row, head), and the
-// exact-partial kernel runs it in the last CTA that finishes a row, so a decode needs no separate merge launch.
+// exact-partial kernel runs it in the last CTA that finishes a row (or a (row, head)), so a decode needs no separate
+// merge launch.
 #pragma once
 #include "kv800_common.cuh"
 

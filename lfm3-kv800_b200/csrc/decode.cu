@@ -1,6 +1,6 @@
 // 800h paged GQA decode on sm_100a: split partials over quantized sub-blocks (qdecode_mma.cuh) and over sinks +
-// exact bf16 tokens (xdecode_mma.cuh), both on the tensor cores, and the log-sum-exp merge with the in-register
-// Hadamard (combine).
+// exact bf16 tokens (xdecode_tma.cuh for the reference's page layout, xdecode_mma.cuh for any other), all on the
+// tensor cores, and the log-sum-exp merge with the in-register Hadamard (combine).
 //
 // Semantics follow the reference's torch decode (lfm3_kv800/torch_decode.py:16-80), including its two bf16 roundings
 // of every key: the dequantized pre-RoPE key is rounded to bf16 (kv800.py:86) and the rotated key is rounded to bf16

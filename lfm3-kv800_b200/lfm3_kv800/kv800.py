@@ -288,8 +288,8 @@ def decode(P, q, cos_t, sin_t, H=None, spb=None, target=None):
 
 def decode_timed(P, q, cos_t, sin_t, spb=None):
     """decode() with CUDA-event timing of its phases (benchmarks; no counterpart in the reference).  Synchronizes.
-    -> (out, {"quantized_ms": schedule + qdecode_mma, "exact_ms": xdecode_mma with the merge of each row's partials
-    (done by the row's last exact-partial CTA), "combine_ms": the gap after it (about zero)})."""
+    -> (out, {"quantized_ms": schedule + qdecode_mma, "exact_ms": the exact partials with the merge of each row's
+    partials (done by the last exact-partial CTA of each row or (row, head)), "combine_ms": the gap after it (about zero)})."""
     ms = (ctypes.c_float * 3)()
     out = _decode(P, q, cos_t, sin_t, spb, None, ms)
     return out, {"quantized_ms": ms[0], "exact_ms": ms[1], "combine_ms": ms[2]}
