@@ -958,11 +958,11 @@ def main():
 def e2e_bench(a, kv800, torch, dist, dev, world, n_gpus, layers, qs, c32, s32):
     """The metric through the public API with host buffers: every step uploads its inputs (6 x q, the current token's
     K / V) from pinned host memory, writes the token into its exact page (kv800.write_exact), decodes (kv800.decode)
-    and reads the 6 outputs back, all inside the timed region.  Copies run on their own stream: all layers' uploads
-    are queued at the step's start, so layer i + 1's inputs arrive while layer i decodes, and layer i's output is
-    read back while layer i + 1 decodes.  The device input buffers are reused across steps: the next step's uploads
-    queue behind this step's last read-back, which waits for the last decode, so no upload overwrites an input still
-    in use."""
+    and reads the 6 outputs back, all inside the timed region.  Uploads and token writes run on their own stream,
+    queued at the step's start, so layer i + 1's inputs arrive and its token lands while layer i decodes; layer i's
+    decode waits for its own layer's write, and its output is read back while layer i + 1 decodes.  The device input
+    buffers and pages are reused across steps: the next step's uploads and writes queue behind this step's last
+    read-back, which waits for the last decode, so nothing overwrites data a decode still reads."""
     B = a.seqs
     nl = len(layers)
     hq = [q.cpu().pin_memory() for q in qs]
@@ -980,14 +980,14 @@ def e2e_bench(a, kv800, torch, dist, dev, world, n_gpus, layers, qs, c32, s32):
 
     def e2e_step():
         with torch.cuda.stream(cps):
-            for i in range(nl):
+            for i, L in enumerate(layers):
                 dq[i].copy_(hq[i], non_blocking=True)
                 dk[i].copy_(hk[i], non_blocking=True)
                 dv[i].copy_(hv[i], non_blocking=True)
+                kv800.write_exact(L.epool, L.eoff, EBS, EBS * 256, 256, 128, dk[i], dv[i], seqs, posv)
                 ready[i].record(cps)
         for i, L in enumerate(layers):
             main_s.wait_event(ready[i])
-            kv800.write_exact(L.epool, L.eoff, EBS, EBS * 256, 256, 128, dk[i], dv[i], seqs, posv)
             o = kv800.decode(L.P, dq[i], c32, s32)
             done[i].record(main_s)
             cps.wait_event(done[i])
