@@ -242,14 +242,15 @@ __device__ __forceinline__ void load16(const uint16_t* row, int e, float* out) {
 
 
 // 2-bit K code round(fl(d / sc)) clamped to [0, 3] (torch's .round().clamp(0, 3) of the IEEE quotient) from the
-// cheap quotient d * (1 / sc): that is within 3 ulp of the IEEE one, so where it is more than 4e-6 (x max(1, |q|))
-// away from the decision points 0.5, 1.5, 2.5 both round alike; near them (and for non-finite q) the IEEE divide
-// decides.
+// cheap quotient q = d * (1 / sc), which is within 3 ulp of the IEEE one.  Only the rounding of quotients in
+// [-0.5, 3.5] can change the clamped code, and there 3 ulp is below 1.5e-6: so where q is farther than 1.6e-5 from a
+// half-integer both round alike, and near one the IEEE divide decides.  Non-finite q fail the distance test and
+// clamp as the IEEE quotient does (NaN to 0, +inf to 3, -inf to 0).
 __device__ __forceinline__ uint32_t code2(float d, float sc, float inv) {
     const float q = d * inv;
-    const float tol = 4e-6f * fmaxf(1.0f, fabsf(q));
-    const bool near = fabsf(q - 0.5f) <= tol || fabsf(q - 1.5f) <= tol || fabsf(q - 2.5f) <= tol || !isfinite(q);
-    return near ? round_clamp(__fdiv_rn(d, sc), 3.0f) : round_clamp(q, 3.0f);
+    const float r = rintf(q);
+    if (fabsf(q - r) > 0.5f - 1.6e-5f) return round_clamp(__fdiv_rn(d, sc), 3.0f);
+    return (uint32_t)fminf(fmaxf(r, 0.0f), 3.0f);
 }
 
 // 1-bit code round(fl(d / sc)) clamped to [0, 1], i.e. [fl(d / sc) > 1/2], from the cheap quotient as in code2.
@@ -392,12 +393,15 @@ __global__ void __launch_bounds__(256) flush_kernel(Src src) {
         __syncwarp();
         // per 2-head group: lo / hi over 256 dims, fp8 lo and scale hi - lo, 1-bit codes.  First from the fast
         // transform: every decision is taken at both ends of the error interval [y - E, y + E] (all of them are
-        // monotone in y), and where both ends agree it is the decision the exact chain gives.  A token with any
-        // undecided byte or bit is redone with the exact chain.
+        // monotone in y), and where both ends agree it is the decision the exact chain gives.  A token with an
+        // undecided scale byte is redone with the exact chain; a token whose only undecided decisions are bits
+        // redoes just those outputs with the chain (hadamard_one).
         uint32_t part[HEADS], lo8[2], sc8[2];
         {
             float y[HEADS][4], E[HEADS];
-            bool ok = fwht_rows(vbuf[warp], y, E);
+            bool ok = fwht_rows(vbuf[warp], y, E);   // finite inputs and the scale bytes decided
+            uint32_t und = 0u;                        // this lane's undecided bits: bit 4 h + k
+            float lofg[2], scfg[2];
 #pragma unroll
             for (int h = 0; h < HEADS; h++) part[h] = 0;
 #pragma unroll
@@ -422,6 +426,8 @@ __global__ void __launch_bounds__(256) flush_kernel(Src src) {
                 sc8[g] = f8enc(clamp_min_1e8(u_lo - l_hi));
                 ok = ok && lo8[g] == f8enc(l_hi) && sc8[g] == f8enc(clamp_min_1e8(u_hi - l_lo));
                 const float lof = f8dec(lo8[g]), scf = clamp_min_1e8(f8dec(sc8[g]));
+                lofg[g] = lof;
+                scfg[g] = scf;
                 const float inv = __frcp_rn(scf);
                 // bit = [fl(fl(y - lo8) / sc8) > 1/2] for the chain's y, which lies within Eg of the estimate:
                 // decided when the estimate's quotient is farther from 1/2 than Eg / sc8 plus the quotient's own error
@@ -431,7 +437,7 @@ __global__ void __launch_bounds__(256) flush_kernel(Src src) {
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
                         const float q = (y[2 * g + hh][k] - lof) * inv;
-                        ok = ok && fabsf(q - 0.5f) > tol * fmaxf(1.0f, fabsf(q));
+                        if (!(fabsf(q - 0.5f) > tol * fmaxf(1.0f, fabsf(q)))) und |= 1u << (4 * (2 * g + hh) + k);
                         part[2 * g + hh] |= (q > 0.5f ? 1u : 0u) << ((lane >> 4) + 2 * k);
                     }
             }
@@ -463,6 +469,21 @@ __global__ void __launch_bounds__(256) flush_kernel(Src src) {
                         for (int k = 0; k < 4; k++)
                             part[2 * g + hh] |= round_clamp(__fdiv_rn(y[2 * g + hh][k] - lof, scf), 1.0f)
                                                 << ((lane >> 4) + 2 * k);
+                }
+            } else if (__any_sync(0xffffffffu, und != 0u)) {
+                // scale bytes decided, some bits not: the exact chain for just those outputs, then the bit as the
+                // exact path takes it (IEEE divide)
+                while (und) {
+                    const int e = __ffs(und) - 1;
+                    und &= und - 1u;
+                    const int h = e >> 2, k = e & 3;
+                    const float yc = hadamard_one(vbuf[warp] + h * DIM, C, k);
+                    const float lof = (h >> 1) ? lofg[1] : lofg[0], scf = (h >> 1) ? scfg[1] : scfg[0];
+                    const uint32_t m = 1u << ((lane >> 4) + 2 * k);
+                    const uint32_t bit = round_clamp(__fdiv_rn(yc - lof, scf), 1.0f) ? m : 0u;
+#pragma unroll
+                    for (int hh = 0; hh < HEADS; hh++)
+                        if (hh == h) part[hh] = (part[hh] & ~m) | bit;
                 }
             }
         }

@@ -46,6 +46,25 @@ __device__ __forceinline__ void hadamard_rows(const float* rows, const float (&C
     }
 }
 
+// One output of hadamard_rows: (x @ H)[lane + 32 k] of the 128 values at row, by the same sequential FMA chain in
+// the same order and with the same operands, so the same bits.  For re-deciding a single element the fast estimate
+// below could not decide.
+__device__ __forceinline__ float hadamard_one(const float* row, const float (&C)[32], int k) {
+    float acc = 0.f;
+#pragma unroll
+    for (int a = 0; a < 4; a++) {
+        const bool neg = (__popc(a & k) & 1) != 0;
+#pragma unroll
+        for (int b4 = 0; b4 < 32; b4 += 4) {
+            const float4 x = *reinterpret_cast<const float4*>(row + 32 * a + b4);
+            const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int u = 0; u < 4; u++) acc = fmaf(neg ? -xs[u] : xs[u], C[b4 + u], acc);
+        }
+    }
+    return acc;
+}
+
 // Fast estimate of the same rotation with a rigorous error bound, for decisions that only need the rotated value to
 // within a tolerance (the quantizer's fp8 lo / scale bytes and 1-bit codes).  y[h][k] ~ (x_h @ H)[lane + 32 k] by a
 // fast Walsh-Hadamard transform (7 butterfly levels, 2 in-lane, 5 across lanes) and one multiply by c, and E[h] bounds
