@@ -290,28 +290,46 @@ static int make_emap(const kv800_paged& P, CUtensorMap& tm) {
     return KV800_OK;
 }
 
+// Host-side preparation of the exact partials (kernel attributes, and the exact pool's tensor map for the
+// tensor-map form, whose encoding is host work of a few microseconds), done before a decode submits its first GPU
+// operation so that its launches reach the stream back to back.
+struct XPrep {
+    bool tma = false;
+    XTArgs ta{};
+};
+static int prepare_xdecode(const XMArgs& xa, XPrep& xp) {
+    xp.tma = xtma_layout(xa.P);
+    if (!xp.tma) return xdecode_setup();
+    int rc = xtma_setup();
+    if (rc) return rc;
+    rc = make_emap(xa.P, xp.ta.tm);
+    if (rc) return rc;
+    xp.ta.x = xa;
+    xp.ta.ehs_rows = xa.P.e_hs / 256;
+    return KV800_OK;
+}
+
 // Launch the exact partials of B rows x nx splits: the tensor-map form (one warp per (row, split, head)) where the
 // layout allows it, else the gather form (a 4-warp CTA per (row, split)).  early: the exact partials do not read the
 // quantized ones (the row merge waits for them).
-static int launch_xdecode(const XMArgs& xa, int64_t B, int nx, cudaStream_t st, bool early = false) {
-    if (xtma_layout(xa.P)) {
-        int rc = xtma_setup();
-        if (rc) return rc;
-        XTArgs ta{};
-        rc = make_emap(xa.P, ta.tm);
-        if (rc) return rc;
-        ta.x = xa;
-        ta.ehs_rows = xa.P.e_hs / 256;
+static void launch_xdecode_prepared(const XPrep& xp, const XMArgs& xa, int64_t B, int nx, cudaStream_t st,
+                                    bool early) {
+    if (xp.tma) {
         LaunchCfg lc(dim3((unsigned)B, (unsigned)nx, HEADS), xt_smem<XT_S>(), st, early, 32);
-        if (xa.cos_t) cudaLaunchKernelEx(&lc.cfg, xdecode_tma<true, XT_S>, ta);
-        else cudaLaunchKernelEx(&lc.cfg, xdecode_tma<false, XT_S>, ta);
-        return KV800_OK;
+        if (xa.cos_t) cudaLaunchKernelEx(&lc.cfg, xdecode_tma<true, XT_S>, xp.ta);
+        else cudaLaunchKernelEx(&lc.cfg, xdecode_tma<false, XT_S>, xp.ta);
+        return;
     }
-    const int rc = xdecode_setup();
-    if (rc) return rc;
     LaunchCfg lc(dim3((unsigned)B, (unsigned)nx), XM_SMEM, st, early);
     if (xa.cos_t) cudaLaunchKernelEx(&lc.cfg, xdecode_mma<true>, xa);
     else cudaLaunchKernelEx(&lc.cfg, xdecode_mma<false>, xa);
+}
+
+static int launch_xdecode(const XMArgs& xa, int64_t B, int nx, cudaStream_t st, bool early = false) {
+    XPrep xp;
+    const int rc = prepare_xdecode(xa, xp);
+    if (rc) return rc;
+    launch_xdecode_prepared(xp, xa, B, nx, st, early);
     return KV800_OK;
 }
 
@@ -384,24 +402,50 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
     float* lo = reinterpret_cast<float*>(ws + pl.lo_off);
     float* ao = reinterpret_cast<float*>(ws + pl.ao_off);
     int* count = reinterpret_cast<int*>(ws + pl.cnt_off);
+    // ---- host-side preparation first (kernel attributes, tensor maps, the slot map), so that the GPU work below
+    // reaches the stream back to back and no device time waits on host encoding
+    const bool needq = pl.persistent || pl.ns > 0;
+    const int64_t rowslots = pl.ns + NX_DEFAULT;
+    QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
+              mo, lo, ao, pl.persistent ? 0 : (int)rowslots, pl.persistent ? 0 : (int)spb, SCALE, status,
+              pl.persistent ? prefix : nullptr, B, 0x40804080u};
+    if (needq) {
+        rc = qdecode_setup();
+        if (rc) return rc;
+        rc = make_qmaps(qa.qpool, qa.qpool_bytes, qa);
+        if (rc) return rc;
+    }
+    SlotMap sm{};
+    sm.nx = NX_DEFAULT;
+    if (pl.persistent) {
+        sm.prefix = prefix;
+        sm.B = B;
+        sm.G0 = pl.G0;
+        sm.xbase = pl.G0 + B;
+        sm.xstride = NX_DEFAULT;
+    } else {
+        sm.ns = (int)pl.ns;
+        sm.qstride = rowslots;
+        sm.xbase = pl.ns;
+        sm.xstride = rowslots;
+    }
+    // the exact partials; the last of a row's NX_DEFAULT CTAs to finish also merges the row's partials into out
+    XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, sm.xbase, sm.xstride, NX_DEFAULT, SCALE, status, count, sm, out};
+    XPrep xp;
+    rc = prepare_xdecode(xa, xp);
+    if (rc) return rc;
+
+    // ---- GPU work
     if (!pl.persistent) {   // (the persistent pass clears them in its schedule scan)
         rc = cuda_status(cudaMemsetAsync(status, 0, pl.cnt_off + 4 * HEADS * B, st),
                          "kv800_decode status / counter reset");
         if (rc) return rc;
     }
     if (ev) cudaEventRecord(ev[0], st);
-    SlotMap sm{};
-    sm.nx = NX_DEFAULT;
     if (pl.persistent) {
-        rc = qdecode_setup();
-        if (rc) return rc;
         qsched_kernel<<<1, 1024, 0, st>>>(P->NQ, P->nqmax, B, prefix, status, (pl.cnt_off + 4 * HEADS * B) / 4);
         rc = cuda_status(cudaGetLastError(), "kv800_decode schedule");
         if (rc) return rc;
-        QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
-                  mo, lo, ao, 0, 0, SCALE, status, prefix, B, 0x40804080u};
-        const int rcm = make_qmaps(qa.qpool, qa.qpool_bytes, qa);
-        if (rcm) return rcm;
         {   // behind the schedule scan, early in untimed calls: the CTAs are placed while the scan runs and wait for
             // its prefix
             LaunchCfg lc(dim3((unsigned)pl.G0), QM_SMEM_TMA, st, !ev);
@@ -409,35 +453,14 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
         }
         rc = cuda_status(cudaGetLastError(), "kv800_decode qdecode");
         if (rc) return rc;
-        sm.prefix = prefix;
-        sm.B = B;
-        sm.G0 = pl.G0;
-        sm.xbase = pl.G0 + B;
-        sm.xstride = NX_DEFAULT;
-    } else {
-        const int64_t rowslots = pl.ns + NX_DEFAULT;
-        if (pl.ns > 0) {
-            rc = qdecode_setup();
-            if (rc) return rc;
-            QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
-                      mo, lo, ao, (int)rowslots, (int)spb, SCALE, status, nullptr, B, 0x40804080u};
-            const int rcm = make_qmaps(qa.qpool, qa.qpool_bytes, qa);
-            if (rcm) return rcm;
-            qdecode_mma<<<dim3((unsigned)B, (unsigned)pl.ns), 128, QM_SMEM_TMA, st>>>(qa);
-            rc = cuda_status(cudaGetLastError(), "kv800_decode qdecode");
-            if (rc) return rc;
-        }
-        sm.ns = (int)pl.ns;
-        sm.qstride = rowslots;
-        sm.xbase = pl.ns;
-        sm.xstride = rowslots;
+    } else if (pl.ns > 0) {
+        qdecode_mma<<<dim3((unsigned)B, (unsigned)pl.ns), 128, QM_SMEM_TMA, st>>>(qa);
+        rc = cuda_status(cudaGetLastError(), "kv800_decode qdecode");
+        if (rc) return rc;
     }
     if (ev) cudaEventRecord(ev[1], st);
-    // the exact partials; the last of a row's NX_DEFAULT CTAs to finish also merges the row's partials into out
-    XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, sm.xbase, sm.xstride, NX_DEFAULT, SCALE, status, count, sm, out};
     // early behind a persistent quantized pass (untimed calls): the exact partials fill the SMs its CTAs leave
-    rc = launch_xdecode(xa, B, NX_DEFAULT, st, pl.persistent && !ev);
-    if (rc) return rc;
+    launch_xdecode_prepared(xp, xa, B, NX_DEFAULT, st, pl.persistent && !ev);
     rc = cuda_status(cudaGetLastError(), "kv800_decode xdecode");
     if (ev) cudaEventRecord(ev[2], st);
     if (ev) cudaEventRecord(ev[3], st);

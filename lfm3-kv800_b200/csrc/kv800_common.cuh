@@ -55,27 +55,27 @@ __device__ __forceinline__ uint16_t f2bf(float f) {
 __device__ __forceinline__ float bfround(float f) { return bf2f(f2bf(f)); }
 
 // fp8 e4m3fn byte -> fp32, exact (bias 7, 3 mantissa bits; e = 0 is the subnormal grid m * 2^-9; 0x7f / 0xff NaN).
+// The magnitude comes from the hardware e4m3 -> f16 conversion (exact: every e4m3 value is an f16 value) and the
+// exact f16 -> f32 widening; the NaN bytes give the canonical quiet NaN and the sign is applied by negation, so -0 and
+// the NaN bits are those of the format-definition decoder.
 __device__ __forceinline__ float f8dec(uint32_t b) {
-    uint32_t e = (b >> 3) & 15u, m = b & 7u;
-    float mag = e ? __uint_as_float(((e + 120u) << 23) | (m << 20)) : (float)m * 0.001953125f;
-    if (e == 15u && m == 7u) mag = __uint_as_float(0x7fc00000u);
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"((unsigned short)(b & 0x7fu)));
+    float mag;
+    asm("{.reg .f16 l, h;\n\tmov.b32 {l, h}, %1;\n\tcvt.f32.f16 %0, l;\n\t}" : "=f"(mag) : "r"(h2));
+    if ((b & 0x7fu) == 0x7fu) mag = __uint_as_float(0x7fc00000u);
     return (b & 0x80u) ? -mag : mag;
 }
 
-// fp32 -> fp8 e4m3fn byte with the semantics of torch's non-saturating cast: round to nearest even, magnitudes above
-// 464 (those that would round past 448), infinities and NaN -> 0x7f with the sign kept.  Written from the format
-// definition: subnormals are the integer multiples of 2^-9 below 2^-6 (exact scaling then RNE), normals round the
-// fp32 mantissa to 3 bits with a carry into the exponent.
+// fp32 -> fp8 e4m3fn byte with the semantics of torch's non-saturating cast: round to nearest even (subnormals on
+// the 2^-9 grid, normals to 3 mantissa bits with a carry into the exponent), magnitudes above 464 (those that would
+// round past 448), infinities and NaN -> 0x7f with the sign kept.  The rounding is the hardware's RNE conversion
+// (cvt.rn.satfinite, the same value converted into both bytes); it is the cast wherever |f| <= 464, where the result
+// is at most 448 and saturation never acts, and the magnitudes above 464 and the NaN take the 0x7f byte explicitly.
 __device__ __forceinline__ uint32_t f8enc(float f) {
-    uint32_t u = __float_as_uint(f);
-    uint32_t sign = (u >> 24) & 0x80u;
-    uint32_t a = u & 0x7fffffffu;
-    float af = __uint_as_float(a);
-    if (a > 0x7f800000u || !(af <= 464.0f)) return sign | 0x7fu;
-    if (af < 0.015625f) return sign | (uint32_t)__float2int_rn(af * 512.0f);
-    uint32_t r = a + 0x7ffffu + ((a >> 20) & 1u);
-    uint32_t e = (r >> 23) - 120u;
-    return sign | (e << 3) | ((r >> 20) & 7u);
+    unsigned short two;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %1;" : "=h"(two) : "f"(f));
+    return (fabsf(f) <= 464.0f) ? (uint32_t)(two & 0xffu) : (((__float_as_uint(f) >> 24) & 0x80u) | 0x7fu);
 }
 
 // torch clamp_min(x, 1e-8): NaN propagates.

@@ -149,3 +149,61 @@ def test_quantizer_stress_matches_oracle(kv800, kind):
     ref = O.quantize_blocks(k, v)
     bad = np.nonzero((got != ref).any(1))[0]
     assert bad.size == 0, f"{kind}: sub-blocks {bad[:8].tolist()} differ"
+
+
+KLO_O, KSC_O = 50176, 50688
+
+
+def test_fp8_bytes_match_torch_cast_on_every_bf16(kv800):
+    """The device fp8 e4m3fn encoder against torch's own fp32 -> float8_e4m3fn cast (the cast of kv800.py:63-64) on
+    every non-NaN bf16 value, infinities and magnitudes past 464 included.  Each value fills one K channel of one
+    sub-block for all 256 tokens, so that channel's lo = hi = the value: its lo byte is the encoder's output for the
+    value, and its scale byte the output for (hi - lo) / 3 clamped at 1e-8 (NaN for the infinities).  A second pass
+    fills each channel with two random finite values (tokens 0..127 and 128..255) so the scale bytes also sweep fp32
+    quotients that are not bf16 values."""
+    bits = np.arange(65536, dtype=np.uint32)
+    f = (bits << 16).view(np.float32)
+    vals = bits[~np.isnan(f)].astype(np.uint16)
+    n = vals.size
+    M = -(-n // 512)
+    ch = np.zeros(M * 512, dtype=np.uint16)
+    ch[:n] = vals
+    k = np.ascontiguousarray(np.broadcast_to(ch.reshape(M, 1, 4, 128), (M, 256, 4, 128)))
+    v = np.zeros_like(k)
+    out = kv800.quantize_blocks(tb(k, DEV), tb(v, DEV)).cpu().numpy()
+    x = torch.from_numpy((ch.astype(np.uint32) << 16).view(np.float32))
+    f8 = torch.float8_e4m3fn
+    np.testing.assert_array_equal(out[:, KLO_O:KSC_O].reshape(-1), x.to(f8).view(torch.uint8).numpy())
+    np.testing.assert_array_equal(out[:, KSC_O:].reshape(-1),
+                                  ((x - x) / 3).clamp_min(1e-8).to(f8).view(torch.uint8).numpy())
+    # two values per channel: lo = min, hi = max, scale = (hi - lo) / 3
+    rs = np.random.RandomState(17)
+    M2 = 64
+    a = I.f32_to_bf16((rs.standard_normal(M2 * 512) * np.exp(rs.uniform(-12, 6, M2 * 512))).astype(np.float32))
+    b = I.f32_to_bf16((rs.standard_normal(M2 * 512) * np.exp(rs.uniform(-12, 6, M2 * 512))).astype(np.float32))
+    k2 = np.empty((M2, 256, 4, 128), dtype=np.uint16)
+    k2[:, :128] = a.reshape(M2, 1, 4, 128)
+    k2[:, 128:] = b.reshape(M2, 1, 4, 128)
+    out2 = kv800.quantize_blocks(tb(k2, DEV), tb(np.zeros_like(k2), DEV)).cpu().numpy()
+    xa = torch.from_numpy((a.astype(np.uint32) << 16).view(np.float32))
+    xb = torch.from_numpy((b.astype(np.uint32) << 16).view(np.float32))
+    lo, hi = torch.minimum(xa, xb), torch.maximum(xa, xb)
+    np.testing.assert_array_equal(out2[:, KLO_O:KSC_O].reshape(-1), lo.to(f8).view(torch.uint8).numpy())
+    np.testing.assert_array_equal(out2[:, KSC_O:].reshape(-1),
+                                  ((hi - lo) / 3).clamp_min(1e-8).to(f8).view(torch.uint8).numpy())
+
+
+def test_fp8_decode_of_every_byte(kv800):
+    """The device fp8 decoder on all 256 bytes: a sub-block whose K codes are 0 and scales 0 dequantizes to
+    K = bf16(0 * 0 + lo) (kv800.py:84-86), compared with the same expression in torch on the float8_e4m3fn -> fp32
+    decode of each byte (NaN bytes: NaN)."""
+    sb = np.zeros((1, 51200), dtype=np.uint8)
+    sb[0, KLO_O:KSC_O] = np.tile(np.arange(256, dtype=np.uint8), 2)
+    kd, _ = kv800.dequantize_blocks(torch.from_numpy(sb).to(DEV))
+    got = kd[0, 0].reshape(-1).float().cpu()
+    lo = torch.from_numpy(np.tile(np.arange(256, dtype=np.uint8), 2)).view(torch.float8_e4m3fn).float()
+    zero = torch.zeros_like(lo)
+    ref = (zero * zero + lo).to(torch.bfloat16).float()   # the reference's codes * ksc + klo (-0 byte -> +0)
+    nan = torch.isnan(ref)
+    assert torch.equal(torch.isnan(got), nan)
+    assert torch.equal(got[~nan].view(torch.int32), ref[~nan].view(torch.int32))
