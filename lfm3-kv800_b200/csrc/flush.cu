@@ -432,12 +432,16 @@ __global__ void __launch_bounds__(256) flush_kernel(Src src) {
                 // bit = [fl(fl(y - lo8) / sc8) > 1/2] for the chain's y, which lies within Eg of the estimate:
                 // decided when the estimate's quotient is farther from 1/2 than Eg / sc8 plus the quotient's own error
                 const float tol = fmaf(Eg, inv * 1.01f, 4e-6f);
+                // one compare per element: |q - 1/2| > 2 tol decides every q the test |q - 1/2| > tol max(1, |q|)
+                // decides when tol < 1/4 (for |q| <= 2 its bound is at most 2 tol; for |q| > 2 both decide, as
+                // |q - 1/2| > 3/2); for larger tol every element is left to the exact chain
+                const float tol2 = tol < 0.25f ? 2.0f * tol : __int_as_float(0x7f800000);
 #pragma unroll
                 for (int hh = 0; hh < 2; hh++)
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
                         const float q = (y[2 * g + hh][k] - lof) * inv;
-                        if (!(fabsf(q - 0.5f) > tol * fmaxf(1.0f, fabsf(q)))) und |= 1u << (4 * (2 * g + hh) + k);
+                        if (!(fabsf(q - 0.5f) > tol2)) und |= 1u << (4 * (2 * g + hh) + k);
                         part[2 * g + hh] |= (q > 0.5f ? 1u : 0u) << ((lane >> 4) + 2 * k);
                     }
             }

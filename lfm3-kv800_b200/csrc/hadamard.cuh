@@ -81,19 +81,37 @@ __device__ __forceinline__ bool fwht_rows(const float* rows, float (&y)[HEADS][4
     const int lane = threadIdx.x & 31;
     const float c = 0.0883883461356163f;
     const float KE = 1.02f * 5.9604644775390625e-08f * 0.0883883461356163f;
+    // this lane's dims d = lane + 32 k of every head, and its part of W + 8 S = sum of (W_i + 8) |x_i|
+    float sl[HEADS];
+#pragma unroll
+    for (int h = 0; h < HEADS; h++) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) y[h][k] = rows[h * DIM + lane + 32 * k];
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; k++) s = fmaf((float)(136 - lane - 32 * k), fabsf(y[h][k]), s);
+        sl[h] = s;
+    }
+    // the 4 sums over the warp in one transposed butterfly: after the xor-16 step a lane keeps heads 2 b4, 2 b4 + 1
+    // (b4 = lane bit 4), after the xor-8 step head 2 b4 + b3, then three plain steps; head h's sum ends in lanes
+    // 8 h .. 8 h + 7 and is broadcast from lane 8 h
+    const bool b4 = (lane & 16) != 0, b3 = (lane & 8) != 0;
+    float k0 = b4 ? sl[2] : sl[0], k1 = b4 ? sl[3] : sl[1];
+    k0 += __shfl_xor_sync(0xffffffffu, b4 ? sl[0] : sl[2], 16);
+    k1 += __shfl_xor_sync(0xffffffffu, b4 ? sl[1] : sl[3], 16);
+    float kk = b3 ? k1 : k0;
+    kk += __shfl_xor_sync(0xffffffffu, b3 ? k0 : k1, 8);
+    kk += __shfl_xor_sync(0xffffffffu, kk, 4);
+    kk += __shfl_xor_sync(0xffffffffu, kk, 2);
+    kk += __shfl_xor_sync(0xffffffffu, kk, 1);
     bool finite = true;
 #pragma unroll
     for (int h = 0; h < HEADS; h++) {
-        float v[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) v[k] = rows[h * DIM + lane + 32 * k];
-        // sum of (W_i + 8) |x_i| with W_i = 128 - i, i = lane + 32 k: W + 8 S in one reduction
-        float s = 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; k++) s = fmaf((float)(136 - lane - 32 * k), fabsf(v[k]), s);
-#pragma unroll
-        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        // dims d = lane + 32 k: bits 5, 6 of d are k (in-lane levels), bits 0..4 are the lane (shuffle levels)
+        const float s = __shfl_sync(0xffffffffu, kk, 8 * h);
+        float v[4] = {y[h][0], y[h][1], y[h][2], y[h][3]};
+        // dims d = lane + 32 k: bits 5, 6 of d are k (in-lane levels), bits 0..4 are the lane (shuffle levels); a
+        // butterfly is one FMA by +-1 (other - v = fma(v, -1, other), v + other = fma(v, 1, other), both exact
+        // products with the one rounding of the sum)
         float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
         v[0] = a0 + a2;
         v[2] = a0 - a2;
@@ -101,11 +119,11 @@ __device__ __forceinline__ bool fwht_rows(const float* rows, float (&y)[HEADS][4
         v[3] = a1 - a3;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const bool upper = (lane & o) != 0;
+            const float sg = (lane & o) ? -1.0f : 1.0f;
 #pragma unroll
             for (int k = 0; k < 4; k++) {
                 const float other = __shfl_xor_sync(0xffffffffu, v[k], o);
-                v[k] = upper ? other - v[k] : v[k] + other;
+                v[k] = fmaf(v[k], sg, other);
             }
         }
 #pragma unroll
