@@ -247,7 +247,7 @@ struct LaunchCfg {
     }
 };
 
-// Stages of the tensor-map form's ring (one warp per CTA; 31 KB of shared memory, seven CTAs per SM).
+// Stages of the tensor-map form's ring (one warp per CTA, 31.5 KB of shared memory with three stages).
 constexpr int XT_S = 3;
 
 static int xtma_setup() {
