@@ -295,6 +295,22 @@ __global__ void __launch_bounds__(256) flush_kernel(Src src) {
                     __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(kr_l), i));
             }
         };
+        {   // every K row of the warp's 32 tokens requested at once (an L2 prefetch of its two 128-byte lines per
+            // lane): the token loops below keep only 4 tokens' loads in flight per warp, and without it the part
+            // waits on DRAM latency
+            const uint16_t *pk, *pv;
+            bool pok;
+            if constexpr (Src::kDirect) {
+                pok = src.rows(m, grp * 32 + lane, h, pk, pv);
+            } else {
+                pk = kr_l;
+                pok = (okm >> lane) & 1u;
+            }
+            if (pok) {
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(pk));
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(pk + 64));
+            }
+        }
 #pragma unroll 4
         for (int i = 0; i < 32; i++) {
             bool ok;
