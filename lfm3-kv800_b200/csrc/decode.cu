@@ -79,6 +79,9 @@ using namespace kv800;
 namespace {
 constexpr int64_t MAX_B = 1 << 20;
 constexpr int NX_DEFAULT = 4;                   // exact splits per row in kv800_decode
+// exact splits per row of a window layer (no quantized sub-blocks): 3 keeps a 64-row layer's 768 one-warp CTAs in
+// one wave on 148 SMs (18.5 us per decode as a CUDA graph, against 20.5 us with 4 splits and 22.0 / 22.5 with 6 / 8)
+constexpr int NX_WIN = 3;
 constexpr float SCALE = 0.12751743074602467f;   // 128^-0.5 * log2(e)
 constexpr int MAX_DEV = 64;
 
@@ -123,6 +126,7 @@ int check_paged(const kv800_paged* P, const char* who) {
 // MO, LO [nslots][16] | AO [nslots][16][128], each 256-byte aligned.
 struct Plan {
     bool persistent;
+    int nx;   // exact splits per row
     int64_t ns, G0, nslots, cnt_off, prefix_off, mo_off, lo_off, ao_off, bytes;
 };
 
@@ -134,7 +138,8 @@ Plan make_plan(int64_t B, int64_t nqmax, int64_t win, int64_t spb) {
     p.persistent = spb <= 0 && nq > 0;
     p.ns = (nq > 0 && !p.persistent) ? (nq + spb - 1) / spb : 0;
     p.G0 = p.persistent ? persistent_ctas() : 0;
-    p.nslots = p.persistent ? p.G0 + B + B * NX_DEFAULT : B * (p.ns + NX_DEFAULT);
+    p.nx = win ? NX_WIN : NX_DEFAULT;
+    p.nslots = p.persistent ? p.G0 + B + B * p.nx : B * (p.ns + p.nx);
     p.cnt_off = 256;
     p.prefix_off = up256(p.cnt_off + 4 * HEADS * B);
     p.mo_off = up256(p.prefix_off + (p.persistent ? (B + 1) * 8 : 0));
@@ -405,7 +410,7 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
     // ---- host-side preparation first (kernel attributes, tensor maps, the slot map), so that the GPU work below
     // reaches the stream back to back and no device time waits on host encoding
     const bool needq = pl.persistent || pl.ns > 0;
-    const int64_t rowslots = pl.ns + NX_DEFAULT;
+    const int64_t rowslots = pl.ns + pl.nx;
     QMArgs qa{q, P->qpool, P->qpool_bytes, P->boff, P->boff_stride, P->NQ, P->nqmax, cos_t, sin_t, npos,
               mo, lo, ao, pl.persistent ? 0 : (int)rowslots, pl.persistent ? 0 : (int)spb, SCALE, status,
               pl.persistent ? prefix : nullptr, B, 0x40804080u};
@@ -416,21 +421,21 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
         if (rc) return rc;
     }
     SlotMap sm{};
-    sm.nx = NX_DEFAULT;
+    sm.nx = pl.nx;
     if (pl.persistent) {
         sm.prefix = prefix;
         sm.B = B;
         sm.G0 = pl.G0;
         sm.xbase = pl.G0 + B;
-        sm.xstride = NX_DEFAULT;
+        sm.xstride = pl.nx;
     } else {
         sm.ns = (int)pl.ns;
         sm.qstride = rowslots;
         sm.xbase = pl.ns;
         sm.xstride = rowslots;
     }
-    // the exact partials; the last of a row's NX_DEFAULT CTAs to finish also merges the row's partials into out
-    XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, sm.xbase, sm.xstride, NX_DEFAULT, SCALE, status, count, sm, out};
+    // the exact partials; the last of a row's pl.nx CTAs to finish also merges the row's partials into out
+    XMArgs xa{q, *P, cos_t, sin_t, npos, mo, lo, ao, sm.xbase, sm.xstride, pl.nx, SCALE, status, count, sm, out};
     XPrep xp;
     rc = prepare_xdecode(xa, xp);
     if (rc) return rc;
@@ -460,7 +465,7 @@ static int decode_core(const kv800_paged* P, const uint16_t* q, const uint16_t* 
     }
     if (ev) cudaEventRecord(ev[1], st);
     // early behind a persistent quantized pass (untimed calls): the exact partials fill the SMs its CTAs leave
-    launch_xdecode_prepared(xp, xa, B, NX_DEFAULT, st, pl.persistent && !ev);
+    launch_xdecode_prepared(xp, xa, B, pl.nx, st, pl.persistent && !ev);
     rc = cuda_status(cudaGetLastError(), "kv800_decode xdecode");
     if (ev) cudaEventRecord(ev[2], st);
     if (ev) cudaEventRecord(ev[3], st);

@@ -108,7 +108,8 @@ def _plan_bytes(B, nqmax, win, spb, G0=444):
     nq = 0 if win else nqmax
     persistent = spb <= 0 and nq > 0
     ns = 0 if (nq == 0 or persistent) else -(-nq // spb)
-    nslots = (G0 + B + 4 * B) if persistent else B * (ns + 4)
+    nx = 3 if win else 4                           # exact splits per row: 3 for window layers, 4 otherwise
+    nslots = (G0 + B + nx * B) if persistent else B * (ns + nx)
     prefix = up(256 + 16 * B)                      # status word | arrival counters per (row, head)
     mo = up(prefix + ((B + 1) * 8 if persistent else 0))
     lo = up(mo + nslots * 64)
