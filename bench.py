@@ -6,9 +6,10 @@ config).  Sub-blocks and exact pages sit at a seeded random permutation of pool 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--windows R] [--impl cuda|reference]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
-A step = the decode of all 6 layers for the rank's 64 sequences (one token per sequence).  Timing: R windows of
-exactly K steps, each bracketed by a barrier and a device synchronize and timed with CUDA events, max over ranks per
-window; `value` = sequences x K x ranks / the median window (tok/s, weak scaling: 64 sequences per GPU), with the
+A step = the decode of all 6 layers for the rank's 64 sequences (one token per sequence), captured once as a CUDA
+graph and replayed (--eager: launched eagerly; the eager median is reported beside the graph's in config.timing).
+Timing: R windows of exactly K steps, each bracketed by a barrier and a device synchronize and timed with CUDA
+events, max over ranks per window; `value` = sequences x K x ranks / the median window (tok/s, weak scaling: 64 sequences per GPU), with the
 windows' spread in config.timing.  Keys of the line:
   e2e          the same metric through the public API with the step's inputs (6 x q, the current token's K / V)
                copied from pinned host memory, the token written into its exact page, and the 6 outputs read back,
@@ -780,6 +781,8 @@ def main():
     ap.add_argument("--check-rows", type=int, default=2, help="rows per GPU checked against the oracle")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--eager", action="store_true",
+                    help="time the step as eager launches instead of one CUDA graph of the 6 layer decodes")
     ap.add_argument("--no-flush", action="store_true", help="skip the quantize / flush measurement")
     ap.add_argument("--no-next", action="store_true", help="skip the vLLM-step / prefill / train / sliding measurement")
     ap.add_argument("--no-config1", action="store_true", help="skip the config 1 measurement")
@@ -834,9 +837,30 @@ def main():
     for _ in range(a.warmup):
         outs = step()
     torch.cuda.synchronize()
+    # the step's 6 layer decodes captured once as a CUDA graph and replayed, as a serving engine replays its decode
+    # step (the decode makes no host sync, so it captures; the launches keep their programmatic dependencies); the
+    # eager step is timed beside it
+    timed_step, graph = step, None
+    if not a.eager:
+        gs = torch.cuda.Stream()
+        gs.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(gs):
+            step()
+            gs.synchronize()
+            with torch.cuda.graph(graph, stream=gs):
+                outs = step()
+        torch.cuda.current_stream().wait_stream(gs)
+        torch.cuda.synchronize()
+        timed_step = graph.replay
+        for _ in range(a.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
     with Clocks(local) as clk:
-        wins = timed_windows(torch, step, a.steps, a.windows, world, dist, dev)
+        wins = timed_windows(torch, timed_step, a.steps, a.windows, world, dist, dev)
     t = statistics.median(wins)
+    wins_eager = wins if graph is None else timed_windows(torch, step, a.steps, max(3, a.windows // 5), world, dist,
+                                                          dev)
     clocks = clk.summary()
     value = a.seqs * a.steps * n_gpus / t
     launches_per_step = sum(3 if L.nq else 1 for L in layers)   # qsched + qdecode + xdecode (merge included)
@@ -942,7 +966,11 @@ def main():
                            "seqs_per_gpu": a.seqs, "ctx": a.ctx, "layers": QUANT_LAYERS + WINDOW_LAYERS,
                            "parallelism": f"dp{n_gpus} (sequence sharding, no collective)",
                            "l2": "inputs larger than L2 (1.87 GB per step); kernel timing flushes L2 per launch",
-                           "timing": window_summary(wins, a.steps)},
+                           "timing": dict(window_summary(wins, a.steps),
+                                          step="eager launches" if graph is None else
+                                          "one CUDA graph of the 6 layer decodes, replayed",
+                                          eager_ms_per_step_median=round(statistics.median(wins_eager) / a.steps
+                                                                         * 1e3, 4))},
                 "hbm_gbs_step": round(step_bytes * a.steps / t / 1e9, 1),
                 "hbm_frac_step": round(step_bytes * a.steps / t / 1e9 / hbm, 4),
                 "bytes_per_step_per_gpu": step_bytes,
